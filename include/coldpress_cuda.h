@@ -1,0 +1,111 @@
+/*
+ * coldpress_cuda.h -- C ABI of libcoldpress_cuda.so, the B200 (sm_100a) encoder hot path of
+ * coldpress: k-quant fit + pack, committed-grid decode, FP64 error-feedback factorisation, the
+ * ordered error-feedback column sweep and X^T X Hessian accumulation.
+ *
+ * Conventions
+ *   - Every array argument is a DEVICE pointer (cudaMalloc / torch CUDA memory), row-major,
+ *     16-byte aligned.  `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *   - Calls only enqueue work; they return before it finishes.  The return value is a
+ *     CP_* status (0 = ok); CP_ERR_CUDA carries the CUDA message in cp_last_error().
+ *   - Types are GGML type ids: Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14.
+ *   - Weights are float32 [nrow, n] with n a multiple of 256 (32 for Q8_0); imatrix vectors
+ *     are float32 [n] and apply to every row; packed rows are n/256 * cp_block_bytes(type).
+ *   - Output bytes are identical to the reference numpy codec (coldpress/kquant.py) for the
+ *     same float32 inputs; inputs containing NaN or Inf are outside that guarantee.
+ *
+ * Line references are to the reference package (coldpress/...), whose Python functions
+ * these entry points replace when coldpress runs with device="cuda".
+ */
+#ifndef COLDPRESS_CUDA_H
+#define COLDPRESS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CP_OK 0
+#define CP_ERR_TYPE 1      /* unsupported GGML type (ef.py:127,176 raise ValueError) */
+#define CP_ERR_SHAPE 2     /* n not a multiple of the block size (kquant.py:351 assert) */
+#define CP_ERR_NOT_PD 3    /* factorisation hit a non-positive pivot (ef.py:74 LinAlgError) */
+#define CP_ERR_CUDA 4      /* a CUDA launch or call failed; see cp_last_error() */
+#define CP_ERR_ARG 5       /* null pointer or out-of-range argument */
+#define CP_ERR_WORKSPACE 6 /* workspace smaller than the matching *_workspace_bytes() */
+
+/* Library version (major*10000 + minor*100 + patch) and the last error message of the
+ * calling thread. */
+int cp_version(void);
+const char* cp_last_error(void);
+
+/* Bytes of one packed block of `ggml_type` (kquant.py:21 BYTES_PER_SB; 34 for Q8_0), or 0. */
+int cp_block_bytes(int ggml_type);
+
+/* kquant.py:732 QUANTIZE[type](x, qw): fit and pack every superblock.  qw == NULL selects
+ * the reference (no imatrix) path.  out: [nrow, n/256 * cp_block_bytes(type)] bytes. */
+int cp_kquant_encode(int ggml_type, const float* x, int64_t nrow, int64_t n, const float* qw,
+                     uint8_t* out, void* stream);
+
+/* kquant.py:734 DEQUANTIZE[type](raw, n): out float32 [nrow, n]. */
+int cp_kquant_decode(int ggml_type, const uint8_t* raw, int64_t nrow, int64_t n, float* out,
+                     void* stream);
+
+/* ef.py:87-127 _grid_params: per (row, sub-block) step dl and offset ml of committed bytes,
+ * float32 [nrow, n/16] (Q2_K, Q3_K, Q6_K) or [nrow, n/32] (Q4_K, Q5_K).  ml may be NULL; it
+ * is written as 0 for the types without a min (Q3_K, Q6_K). */
+int cp_grid_params(int ggml_type, const uint8_t* raw, int64_t nrow, int64_t n, float* dl, float* ml,
+                   void* stream);
+
+/* Signed integer codes held by committed bytes (ef.py's L: Q2_K 0..3, Q3_K -4..3, Q4_K 0..15,
+ * Q5_K 0..31, Q6_K -32..31) as int8 [nrow, n]. */
+int cp_kquant_codes(int ggml_type, const uint8_t* raw, int64_t nrow, int64_t n, int8_t* codes,
+                    void* stream);
+
+/* ef.py:130-176 _repack: write int8 codes [nrow, n] into committed bytes, scales unchanged. */
+int cp_kquant_repack(int ggml_type, uint8_t* raw, const int8_t* codes, int64_t nrow, int64_t n,
+                     void* stream);
+
+/* ef.py:46-84 cholesky_inv_upper with ef.py:187-189 folded in: for the act-order permutation
+ * `order` (int32 [n]), U_out = float32(chol(inv(H[order][:,order] + diag_shift*I)).T), upper
+ * triangular [n, n].  diag_shift is the reference's damp*mean(diag(H[order][:,order])) + 1e-8.
+ * H: float64 [n, n] symmetric, n a multiple of 64.  *status_dev (device int32) is set to 0,
+ * or to CP_ERR_NOT_PD when a pivot is not positive; callers escalate damp and retry as
+ * ef.py:67-76 does.  workspace >= cp_factor_workspace_bytes(n). */
+size_t cp_factor_workspace_bytes(int64_t n);
+int cp_factor_u(const double* H, int64_t n, const int32_t* order, double diag_shift, float* U_out,
+                void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
+/* Same factor left in float64 (ef.py:46-84 returns float64; ef_encode casts it). */
+int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double diag_shift, double* U_out,
+                    void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
+
+/* ef.py:179-218 ef_encode given U (the float32 factor above) and the act-order permutation:
+ * n_iter rounds of {commit grid with QUANTIZE(w_cur, qw); ordered column sweep; repack}.
+ * out: packed bytes as cp_kquant_encode.  first_fit_out (optional, may be NULL) receives the
+ * first round's committed bytes, which equal QUANTIZE(x, qw) (encode_gguf's stock baseline,
+ * ef.py:298).  workspace >= cp_ef_workspace_bytes(type, nrow, n). */
+size_t cp_ef_workspace_bytes(int ggml_type, int64_t nrow, int64_t n);
+int cp_ef_encode(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
+                 const float* U, const float* qw, int n_iter, uint8_t* out, uint8_t* first_fit_out,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* One error-feedback pass (ef.py:197-216) against committed grid (dl, ml from
+ * cp_grid_params): codes int8 [nrow, n] in storage order; w_out (optional) receives the
+ * compensated weights un-permuted (ef.py:215-216).  UT2 and diagU come from
+ * cp_ef_prepare_u.  workspace >= cp_ef_sweep_workspace_bytes(nrow, n). */
+size_t cp_ef_u_bytes(int64_t n);
+int cp_ef_prepare_u(const float* U, int64_t n, float* ut2_and_diag, void* stream);
+size_t cp_ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
+int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
+                const float* U, const float* ut2_and_diag, const float* dl, const float* ml,
+                int8_t* codes, float* w_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* hessians.py:455-470 hook arithmetic: H += x^T x for x bf16 [T, d] (row-major, d a
+ * multiple of 128), H float32 [d, d], accumulated in float32 on the tensor cores. */
+int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* COLDPRESS_CUDA_H */

@@ -1,0 +1,214 @@
+// extern "C" entry points of libcoldpress_cuda.so (declared in include/coldpress_cuda.h).
+// Argument checks and workspace carving live here; the kernels are in the other units.
+#include <cuda_runtime.h>
+#include <cstdio>
+#include <cstring>
+#include "../../include/coldpress_cuda.h"
+#include "ef_kernels.h"
+#include "kq_common.cuh"
+#include "kquant_kernels.h"
+#include "xtx_kernels.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int set_err(int code, const char* msg) {
+  std::snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    std::snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+    return CP_ERR_CUDA;
+  }
+  return CP_OK;
+}
+
+int check_rc(int rc, const char* what) {
+  if (rc == 1) return set_err(CP_ERR_TYPE, what);
+  if (rc == 2) return set_err(CP_ERR_SHAPE, what);
+  if (rc != 0) return set_err(CP_ERR_ARG, what);
+  return check_launch(what);
+}
+
+bool is_k_type(int t) { return t == cpk::kQ2_K || t == cpk::kQ3_K || t == cpk::kQ4_K || t == cpk::kQ5_K || t == cpk::kQ6_K; }
+
+int check_shape(int t, int64_t nrow, int64_t n, bool allow_q80) {
+  if (!(is_k_type(t) || (allow_q80 && t == cpk::kQ8_0)))
+    return set_err(CP_ERR_TYPE, "unsupported ggml type (k-quants Q2_K..Q6_K, and Q8_0 where noted)");
+  const int64_t blk = (t == cpk::kQ8_0) ? 32 : 256;
+  if (nrow < 0 || n <= 0 || n % blk) return set_err(CP_ERR_SHAPE, "n must be a positive multiple of the block size");
+  if (nrow > (int64_t)1 << 31 || n > (int64_t)1 << 30) return set_err(CP_ERR_SHAPE, "tensor too large");
+  return CP_OK;
+}
+
+size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+struct EfLayout {
+  size_t ut2, sweep, wcur, dl, ml, codes, total;
+};
+
+EfLayout ef_layout(int t, int64_t nrow, int64_t n) {
+  int sbw = 16, lo, hi;
+  bool hm;
+  cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
+  EfLayout L;
+  size_t off = 0;
+  L.ut2 = off; off += align256(cpk::ef_ut2_bytes(n));
+  L.sweep = off; off += align256(cpk::ef_sweep_workspace_bytes(nrow, n));
+  L.wcur = off; off += align256((size_t)nrow * n * sizeof(float));
+  L.dl = off; off += align256((size_t)nrow * (n / sbw) * sizeof(float));
+  L.ml = off; off += align256((size_t)nrow * (n / sbw) * sizeof(float));
+  L.codes = off; off += align256((size_t)nrow * n);
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cp_version(void) { return 100; }
+
+const char* cp_last_error(void) { return g_err; }
+
+int cp_block_bytes(int ggml_type) { return cpk::block_bytes(ggml_type); }
+
+int cp_kquant_encode(int t, const float* x, int64_t nrow, int64_t n, const float* qw, uint8_t* out, void* stream) {
+  if (int rc = check_shape(t, nrow, n, true)) return rc;
+  if ((!x || !out) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
+  if (((uintptr_t)x | (uintptr_t)qw) & 15) return set_err(CP_ERR_ARG, "x and qw must be 16-byte aligned");
+  if (t != cpk::kQ8_0 && ((uintptr_t)out & 15)) return set_err(CP_ERR_ARG, "out must be 16-byte aligned");
+  return check_rc(cpk::launch_quantize(t, x, nrow, n, qw, out, (cudaStream_t)stream), "cp_kquant_encode");
+}
+
+int cp_kquant_decode(int t, const uint8_t* raw, int64_t nrow, int64_t n, float* out, void* stream) {
+  if (int rc = check_shape(t, nrow, n, true)) return rc;
+  if ((!raw || !out) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_dequantize(t, raw, nrow, n, out, (cudaStream_t)stream), "cp_kquant_decode");
+}
+
+int cp_grid_params(int t, const uint8_t* raw, int64_t nrow, int64_t n, float* dl, float* ml, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if ((!raw || !dl) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_grid_params(t, raw, nrow, n, dl, ml, (cudaStream_t)stream), "cp_grid_params");
+}
+
+int cp_kquant_codes(int t, const uint8_t* raw, int64_t nrow, int64_t n, int8_t* codes, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if ((!raw || !codes) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_codes(t, raw, nrow, n, codes, (cudaStream_t)stream), "cp_kquant_codes");
+}
+
+int cp_kquant_repack(int t, uint8_t* raw, const int8_t* codes, int64_t nrow, int64_t n, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if ((!raw || !codes) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_repack(t, raw, codes, nrow, n, (cudaStream_t)stream), "cp_kquant_repack");
+}
+
+size_t cp_factor_workspace_bytes(int64_t n) { return n > 0 ? cpk::factor_workspace_bytes(n) : 0; }
+
+static int factor_common(const double* H, int64_t n, const int32_t* order, double diag_shift, void* U_out,
+                         bool f64, void* workspace, size_t ws_bytes, int32_t* status_dev, void* stream) {
+  if (n <= 0 || n % 64) return set_err(CP_ERR_SHAPE, "n must be a positive multiple of 64");
+  if (n > 65536) return set_err(CP_ERR_SHAPE, "n too large");
+  if (!H || !order || !U_out || !workspace || !status_dev) return set_err(CP_ERR_ARG, "null pointer");
+  if (ws_bytes < cpk::factor_workspace_bytes(n)) return set_err(CP_ERR_WORKSPACE, "factor workspace too small");
+  return check_rc(cpk::launch_factor_u(H, n, order, diag_shift, U_out, f64, workspace, status_dev,
+                                       (cudaStream_t)stream),
+                  "cp_factor_u");
+}
+
+int cp_factor_u(const double* H, int64_t n, const int32_t* order, double diag_shift, float* U_out, void* workspace,
+                size_t ws_bytes, int32_t* status_dev, void* stream) {
+  return factor_common(H, n, order, diag_shift, U_out, false, workspace, ws_bytes, status_dev, stream);
+}
+
+int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double diag_shift, double* U_out,
+                    void* workspace, size_t ws_bytes, int32_t* status_dev, void* stream) {
+  return factor_common(H, n, order, diag_shift, U_out, true, workspace, ws_bytes, status_dev, stream);
+}
+
+size_t cp_ef_u_bytes(int64_t n) { return n > 0 ? cpk::ef_ut2_bytes(n) : 0; }
+
+int cp_ef_prepare_u(const float* U, int64_t n, float* ut2_and_diag, void* stream) {
+  if (n <= 0 || n % 256) return set_err(CP_ERR_SHAPE, "n must be a positive multiple of 256");
+  if (!U || !ut2_and_diag) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_build_ut2(U, n, ut2_and_diag, ut2_and_diag + (size_t)n * n, (cudaStream_t)stream),
+                  "cp_ef_prepare_u");
+}
+
+size_t cp_ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
+  return (nrow > 0 && n > 0) ? cpk::ef_sweep_workspace_bytes(nrow, n) : 0;
+}
+
+int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* U,
+                const float* ut2, const float* dl, const float* ml, int8_t* codes, float* w_out, void* workspace,
+                size_t ws_bytes, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if (nrow == 0) return CP_OK;
+  int sbw, lo, hi;
+  bool hm;
+  cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
+  if (!x || !order || !U || !ut2 || !dl || (hm && !ml) || !codes || !workspace) return set_err(CP_ERR_ARG, "null pointer");
+  if (ws_bytes < cpk::ef_sweep_workspace_bytes(nrow, n)) return set_err(CP_ERR_WORKSPACE, "sweep workspace too small");
+  return check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, U, ut2, ut2 + (size_t)n * n, dl, ml, workspace, codes,
+                                       w_out, (cudaStream_t)stream),
+                  "cp_ef_sweep");
+}
+
+size_t cp_ef_workspace_bytes(int t, int64_t nrow, int64_t n) {
+  if (!is_k_type(t) || nrow <= 0 || n <= 0) return 0;
+  return ef_layout(t, nrow, n).total;
+}
+
+int cp_ef_encode(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* U, const float* qw,
+                 int n_iter, uint8_t* out, uint8_t* first_fit_out, void* workspace, size_t ws_bytes, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if (nrow == 0) return CP_OK;
+  if (n_iter < 1 || n_iter > 64) return set_err(CP_ERR_ARG, "n_iter must be in 1..64");
+  if (!x || !order || !U || !out || !workspace) return set_err(CP_ERR_ARG, "null pointer");
+  if (((uintptr_t)x | (uintptr_t)qw | (uintptr_t)out | (uintptr_t)workspace) & 15)
+    return set_err(CP_ERR_ARG, "x, qw, out and workspace must be 16-byte aligned");
+  const EfLayout L = ef_layout(t, nrow, n);
+  if (ws_bytes < L.total) return set_err(CP_ERR_WORKSPACE, "ef workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  float* ut2 = (float*)(ws + L.ut2);
+  float* wcur = (float*)(ws + L.wcur);
+  float* dl = (float*)(ws + L.dl);
+  float* ml = (float*)(ws + L.ml);
+  int8_t* codes = (int8_t*)(ws + L.codes);
+  int rc;
+  if ((rc = check_rc(cpk::launch_build_ut2(U, n, ut2, ut2 + (size_t)n * n, s), "cp_ef_encode: U layout"))) return rc;
+  for (int it = 0; it < n_iter; it++) {
+    // commit the grid from the current (compensated) weights; round 1 starts from x
+    const float* src = it == 0 ? x : wcur;
+    if ((rc = check_rc(cpk::launch_quantize(t, src, nrow, n, qw, out, s), "cp_ef_encode: fit"))) return rc;
+    if (it == 0 && first_fit_out) {
+      const size_t nb = (size_t)nrow * (n / 256) * cpk::block_bytes(t);
+      if (cudaMemcpyAsync(first_fit_out, out, nb, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return check_launch("cp_ef_encode: first-fit copy");
+    }
+    if ((rc = check_rc(cpk::launch_grid_params(t, out, nrow, n, dl, ml, s), "cp_ef_encode: grid"))) return rc;
+    if ((rc = check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, U, ut2, ut2 + (size_t)n * n, dl, ml, ws + L.sweep,
+                                            codes, it + 1 < n_iter ? wcur : nullptr, s),
+                       "cp_ef_encode: sweep")))
+      return rc;
+    if ((rc = check_rc(cpk::launch_repack(t, out, codes, nrow, n, s), "cp_ef_encode: repack"))) return rc;
+  }
+  return CP_OK;
+}
+
+int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream) {
+  if (T < 0 || d <= 0 || d % 128) return set_err(CP_ERR_SHAPE, "d must be a positive multiple of 128");
+  if (T == 0) return CP_OK;
+  if (!x_bf16 || !H) return set_err(CP_ERR_ARG, "null pointer");
+  if (((uintptr_t)x_bf16 | (uintptr_t)H) & 15) return set_err(CP_ERR_ARG, "x and H must be 16-byte aligned");
+  return check_rc(cpk::launch_xtx(x_bf16, T, d, H, (cudaStream_t)stream), "cp_xtx_accumulate");
+}
+
+}  // extern "C"

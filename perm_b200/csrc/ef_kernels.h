@@ -1,0 +1,17 @@
+// Internal launcher declarations for the error-feedback path (sweep, U layout, factorisation).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace cpk {
+size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
+size_t ef_ut2_bytes(int64_t n);
+int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream);
+int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* U,
+                    const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
+                    int8_t* codes, float* wcur, cudaStream_t stream);
+size_t factor_workspace_bytes(int64_t n);
+int launch_factor_u(const double* H, int64_t n, const int* order, double shift, void* U, bool out_f64,
+                    void* work, int* status, cudaStream_t stream);
+}  // namespace cpk

@@ -1,0 +1,297 @@
+// FP64 factorization for error feedback: U = chol(inv(Hd)).T, the upper-triangular factor of
+// coldpress/ef.py:46-84 (cholesky_inv_upper) cast to float32, computed on the GPU as
+//     P  = J * Hd[order][:, order] * J          (act-order permutation, then reversal J)
+//     P  = L L^T                                (blocked right-looking Cholesky, nb = 64)
+//     U  = J * L^{-1} * J                       (blocked triangular inverse, then reversal)
+// Because Hd = (J L J)(J L J)^T with J L J upper, (J L^{-1} J) is the unique upper factor
+// with U^T U = inv(Hd): the same matrix as the reference's inv-then-cholesky route, in one
+// Cholesky plus one triangular inverse.  Every step stays in float64 so the float32 cast
+// matches the reference's cast.  A non-positive pivot sets a status word (no trap); the host
+// then escalates the damping exactly like the reference does.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "ef_kernels.h"
+
+namespace cpk {
+
+constexpr int NB = 64;
+
+// P[i][j] = H[order[n-1-i]][order[n-1-j]] (+ shift on the diagonal).  Only the lower
+// triangle is consumed; the strict upper triangle is written as zero.
+__global__ void permute_reverse_kernel(const double* __restrict__ H, int n, const int* __restrict__ order,
+                                       double shift, double* __restrict__ P) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+  if (j >= n) return;
+  double v = 0.0;
+  if (j <= i) {
+    v = H[(size_t)order[n - 1 - i] * n + order[n - 1 - j]];
+    if (i == j) v += shift;
+  }
+  P[(size_t)i * n + j] = v;
+}
+
+// In-place Cholesky of the nb x nb diagonal block at (k, k); also writes its inverse (lower)
+// into Dinv.  One CTA of 256 threads.  status != 0 stops the factorisation.
+__global__ void potrf_diag_kernel(double* __restrict__ A, int n, int k, double* __restrict__ Dinv,
+                                  int* __restrict__ status) {
+  __shared__ double a[NB][NB + 1];
+  __shared__ int bad;
+  const int t = threadIdx.x;
+  const int nb = min(NB, n - k);
+  if (t == 0) bad = *status;
+  for (int i = t; i < NB * NB; i += blockDim.x) {
+    const int r = i / NB, c = i % NB;
+    a[r][c] = (r < nb && c <= r) ? A[(size_t)(k + r) * n + k + c] : (r == c ? 1.0 : 0.0);
+  }
+  __syncthreads();
+  if (bad) return;
+  for (int j = 0; j < nb; j++) {
+    if (t == 0) {
+      const double d = a[j][j];
+      if (!(d > 0.0)) bad = 1;  // not positive definite (or NaN)
+      else a[j][j] = sqrt(d);
+    }
+    __syncthreads();
+    if (bad) break;
+    const double djj = a[j][j];
+    for (int r = j + 1 + t; r < nb; r += blockDim.x) a[r][j] /= djj;
+    __syncthreads();
+    for (int i = t; i < (nb - j - 1) * (nb - j - 1); i += blockDim.x) {
+      const int r = j + 1 + i / (nb - j - 1), c = j + 1 + i % (nb - j - 1);
+      if (c <= r) a[r][c] -= a[r][j] * a[c][j];
+    }
+    __syncthreads();
+  }
+  if (bad) {
+    if (t == 0) *status = 1;
+    return;
+  }
+  // inverse of the lower-triangular block: column c solved by forward substitution
+  for (int c = t; c < NB; c += blockDim.x) {
+    double col[NB];
+    for (int r = 0; r < NB; r++) {
+      if (r < c) { col[r] = 0.0; continue; }
+      double s = (r == c) ? 1.0 : 0.0;
+      for (int l = c; l < r; l++) s -= a[r][l] * col[l];
+      col[r] = s / a[r][r];
+    }
+    for (int r = 0; r < NB; r++) Dinv[r * NB + c] = col[r];
+  }
+  for (int i = t; i < NB * NB; i += blockDim.x) {
+    const int r = i / NB, c = i % NB;
+    if (r < nb && c < nb) A[(size_t)(k + r) * n + k + c] = (c <= r) ? a[r][c] : 0.0;
+  }
+}
+
+// Tile GEMM: C[64x64 tile] = alpha * sum_l A[i][l] * Bop[l][j] (+ beta * C), FP64 on CUDA
+// cores, 256 threads with a 4x4 register tile each, K streamed in chunks of 16 through
+// shared memory.  B_TRANS: Bop[l][j] = B[j][l] (A*B^T), else Bop[l][j] = B[l][j].
+template <bool B_TRANS>
+__device__ __forceinline__ void tile_gemm(const double* __restrict__ A, int lda, const double* __restrict__ B,
+                                          int ldb, int m_lim, int n_lim, int k_len, double (&acc)[4][4]) {
+  __shared__ double sa[16][64 + 1];
+  __shared__ double sb[16][64 + 1];
+  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+  for (int l0 = 0; l0 < k_len; l0 += 16) {
+    for (int i = t; i < 16 * 64; i += 256) {
+      const int r = i / 16, l = i % 16;  // A row r, column l0+l
+      sa[l][r] = (r < m_lim && l0 + l < k_len) ? A[(size_t)r * lda + l0 + l] : 0.0;
+    }
+    if (B_TRANS) {
+      for (int i = t; i < 16 * 64; i += 256) {
+        const int c = i / 16, l = i % 16;
+        sb[l][c] = (c < n_lim && l0 + l < k_len) ? B[(size_t)c * ldb + l0 + l] : 0.0;
+      }
+    } else {
+      for (int i = t; i < 16 * 64; i += 256) {
+        const int l = i / 64, c = i % 64;
+        sb[l][c] = (c < n_lim && l0 + l < k_len) ? B[(size_t)(l0 + l) * ldb + c] : 0.0;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int l = 0; l < 16; l++) {
+      double av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) av[i] = sa[l][tr + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) bv[j] = sb[l][tc + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+}
+
+// Panel below the diagonal block: A21 := A21 * inv(L11)^T.
+__global__ void __launch_bounds__(256) trsm_panel_kernel(double* __restrict__ A, int n, int k,
+                                                         const double* __restrict__ Dinv, const int* status) {
+  if (*status) return;
+  const int r0 = k + NB + blockIdx.x * 64;
+  const int m = min(64, n - r0);
+  const int nb = min(NB, n - k);
+  double acc[4][4];
+  // out[r][c] = sum_l A21[r][l] * Dinv[c][l]
+  tile_gemm<true>(A + (size_t)r0 * n + k, n, Dinv, NB, m, nb, nb, acc);
+  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int r = tr + 16 * i, c = tc + 16 * j;
+      if (r < m && c < nb) A[(size_t)(r0 + r) * n + k + c] = acc[i][j];
+    }
+}
+
+// Trailing update A22 -= A21 A21^T on lower 64x64 tiles.
+__global__ void __launch_bounds__(256) syrk_kernel(double* __restrict__ A, int n, int k, const int* status) {
+  if (*status) return;
+  // blockIdx.x enumerates lower tiles (ti >= tj) of the trailing matrix
+  int idx = blockIdx.x, ti = 0;
+  while (idx > ti) { idx -= ti + 1; ti++; }
+  const int tj = idx;
+  const int base = k + NB;
+  const int r0 = base + ti * 64, c0 = base + tj * 64;
+  const int m = min(64, n - r0), nn = min(64, n - c0);
+  double acc[4][4];
+  tile_gemm<true>(A + (size_t)r0 * n + k, n, A + (size_t)c0 * n + k, n, m, nn, NB, acc);
+  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int r = tr + 16 * i, c = tc + 16 * j;
+      if (r < m && c < nn && r0 + r >= c0 + c) A[(size_t)(r0 + r) * n + c0 + c] -= acc[i][j];
+    }
+}
+
+// Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
+//   T   = -Linv22 * L21          (rows below, into scratch)
+__global__ void __launch_bounds__(256) trmm_kernel(const double* __restrict__ A, int n, int j,
+                                                   double* __restrict__ T, const int* status) {
+  if (*status) return;
+  const int base = j + NB;
+  const int r0 = base + blockIdx.x * 64;
+  const int m = min(64, n - r0);
+  // rows r0.. of Linv22 have nonzeros only in columns base .. r0+m-1
+  const int k_len = r0 + m - base;
+  double acc[4][4];
+  tile_gemm<false>(A + (size_t)r0 * n + base, n, A + (size_t)base * n + j, n, m, NB, k_len, acc);
+  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int r = tr + 16 * i, cc = tc + 16 * c;
+      if (r < m) T[(size_t)(r0 - base + r) * NB + cc] = -acc[i][c];
+    }
+}
+
+//   L21 := T * inv(L11)  and  L11 := inv(L11)
+__global__ void __launch_bounds__(256) trinv_apply_kernel(double* __restrict__ A, int n, int j,
+                                                          const double* __restrict__ T,
+                                                          const double* __restrict__ Dinv, const int* status) {
+  if (*status) return;
+  const int base = j + NB;
+  if ((int)blockIdx.x * 64 + base >= n) {
+    // the extra CTA writes the inverted diagonal block
+    for (int i = threadIdx.x; i < NB * NB; i += blockDim.x) {
+      const int r = i / NB, c = i % NB;
+      if (j + r < n && j + c < n) A[(size_t)(j + r) * n + j + c] = Dinv[i];
+    }
+    return;
+  }
+  const int r0 = base + blockIdx.x * 64;
+  const int m = min(64, n - r0);
+  double acc[4][4];
+  tile_gemm<false>(T + (size_t)(r0 - base) * NB, NB, Dinv, NB, m, NB, NB, acc);
+  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int r = tr + 16 * i, cc = tc + 16 * c;
+      if (r < m) A[(size_t)(r0 + r) * n + j + cc] = acc[i][c];
+    }
+}
+
+// Inverse of the (already factorised, lower) diagonal block at (j, j) into Dinv.
+__global__ void trti2_kernel(const double* __restrict__ A, int n, int j, double* __restrict__ Dinv,
+                             const int* status) {
+  if (*status) return;
+  __shared__ double a[NB][NB + 1];
+  const int t = threadIdx.x;
+  for (int i = t; i < NB * NB; i += blockDim.x) {
+    const int r = i / NB, c = i % NB;
+    a[r][c] = (c <= r) ? A[(size_t)(j + r) * n + j + c] : 0.0;
+  }
+  __syncthreads();
+  for (int c = t; c < NB; c += blockDim.x) {
+    double col[NB];
+    for (int r = 0; r < NB; r++) {
+      if (r < c) { col[r] = 0.0; continue; }
+      double s = (r == c) ? 1.0 : 0.0;
+      for (int l = c; l < r; l++) s -= a[r][l] * col[l];
+      col[r] = s / a[r][r];
+    }
+    for (int r = 0; r < NB; r++) Dinv[r * NB + c] = col[r];
+  }
+}
+
+// U[i][j] = Linv[n-1-i][n-1-j] for j >= i, else 0 (cast to OutT).
+template <typename OutT>
+__global__ void unreverse_cast_kernel(const double* __restrict__ Linv, int n, OutT* __restrict__ U) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+  if (j >= n) return;
+  U[(size_t)i * n + j] = (j >= i) ? (OutT)Linv[(size_t)(n - 1 - i) * n + (n - 1 - j)] : (OutT)0;
+}
+
+size_t factor_workspace_bytes(int64_t n) {
+  // P (n x n f64) + Dinv (nb x nb) + T (n x nb)
+  return ((size_t)n * n + (size_t)NB * NB + (size_t)n * NB) * sizeof(double);
+}
+
+int launch_factor_u(const double* H, int64_t n64, const int* order, double shift, void* U, bool out_f64,
+                    void* work, int* status, cudaStream_t stream) {
+  if (n64 <= 0 || n64 % NB) return 2;
+  const int n = (int)n64;
+  double* P = (double*)work;
+  double* Dinv = P + (size_t)n * n;
+  double* T = Dinv + NB * NB;
+  cudaMemsetAsync(status, 0, sizeof(int), stream);
+  {
+    dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
+    permute_reverse_kernel<<<g, 256, 0, stream>>>(H, n, order, shift, P);
+  }
+  for (int k = 0; k < n; k += NB) {
+    potrf_diag_kernel<<<1, 256, 0, stream>>>(P, n, k, Dinv, status);
+    const int rem = n - k - NB;
+    if (rem > 0) {
+      const int tiles = (rem + 63) / 64;
+      trsm_panel_kernel<<<tiles, 256, 0, stream>>>(P, n, k, Dinv, status);
+      syrk_kernel<<<tiles * (tiles + 1) / 2, 256, 0, stream>>>(P, n, k, status);
+    }
+  }
+  // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower)
+  for (int j = n - NB; j >= 0; j -= NB) {
+    trti2_kernel<<<1, 64, 0, stream>>>(P, n, j, Dinv, status);
+    const int rem = n - j - NB;
+    const int tiles = (rem + 63) / 64;
+    if (rem > 0) trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+    trinv_apply_kernel<<<tiles + 1, 256, 0, stream>>>(P, n, j, T, Dinv, status);
+  }
+  {
+    dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
+    if (out_f64) unreverse_cast_kernel<double><<<g, 256, 0, stream>>>(P, n, (double*)U);
+    else unreverse_cast_kernel<float><<<g, 256, 0, stream>>>(P, n, (float*)U);
+  }
+  return 0;
+}
+
+}  // namespace cpk

@@ -1,0 +1,311 @@
+// Per-thread k-quant block fitters: one thread fits one sub-block held in registers.
+// Each function restates one numpy fitter of coldpress/kquant.py with the same operation
+// order, so results are bit-identical (translation units are built with -fmad=false).
+#pragma once
+#include "kq_common.cuh"
+
+namespace cpk {
+
+// make_qkx_quants (kquant.py:42-94): asymmetric (scale, min) search over nstep+1 candidate
+// inverse scales, weighted least squares per candidate, accept on lower weighted error.
+// Instead of copying the candidate codes on acceptance, the (iscale, min) pair that produced
+// them is recorded and the codes are recomputed once at the end (same arithmetic).
+// Outputs: scale, -min and the codes as floats (0..nmax).
+template <int N, bool MAD, bool QKX3>
+__device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N], int nmax, float rmin,
+                                        float rdelta, int nstep, float& o_scale, float& o_negmin,
+                                        float (&Lf)[N]) {
+  float mn = x[0], mx = x[0];
+#pragma unroll
+  for (int i = 1; i < N; i++) {
+    mn = np_min_step(mn, x[i]);
+    mx = np_max_step(mx, x[i]);
+  }
+  Pw8 pw, px;
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    pw.addi(i, w[i]);
+    px.addi(i, w[i] * x[i]);
+  }
+  const float sum_w = pw.total();
+  const float sum_x = px.total();
+  mn = np_minimum(mn, 0.0f);
+  const bool dead = QKX3 ? (mx <= mn) : (mx == mn);
+  const float span = dead ? 1.0f : mx - mn;
+  const float iscale = (float)nmax / span;
+  float scale = 1.0f / iscale;
+  // An infinite inverse scale makes numpy's codes all 0 (inf, -inf and the x86 default NaN
+  // all clip to the low end); reproduce that explicitly.
+  const bool fin0 = iscale <= 3.4028234663852886e38f;
+  float best;
+  {
+    Pw8 pb;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      float l = fin0 ? nint_clip_f(iscale * (x[i] - mn), 0, nmax) : 0.0f;
+      float d = scale * l + mn - x[i];
+      d = MAD ? fabsf(d) : d * d;
+      pb.addi(i, w[i] * d);
+    }
+    best = pb.total();
+  }
+  float b_isc = iscale, b_mn = mn;
+  bool b_fin = fin0;
+  float lf[N];
+  for (int step = 0; step <= nstep; step++) {
+    float span_cur = mx - mn;
+    span_cur = span_cur > 0.0f ? span_cur : 1.0f;
+    const float isc = (rmin + rdelta * (float)step + (float)nmax) / span_cur;
+    Pw8 sl, sl2, sxl;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      lf[i] = nint_clip_f(isc * (x[i] - mn), 0, nmax);
+      const float wl = w[i] * lf[i];
+      sl.addi(i, wl);
+      sl2.addi(i, wl * lf[i]);
+      sxl.addi(i, wl * x[i]);
+    }
+    const float sum_l = sl.total(), sum_l2 = sl2.total(), sum_xl = sxl.total();
+    const float D = sum_w * sum_l2 - sum_l * sum_l;
+    // numpy: an infinite candidate scale gives all-zero codes, hence D == 0: never accepted.
+    const bool ok = D > 0.0f && isc <= 3.4028234663852886e38f;
+    if (ok && !dead) {
+      float this_scale = (sum_w * sum_xl - sum_x * sum_l) / D;
+      float this_min = (sum_l2 * sum_x - sum_l * sum_xl) / D;
+      const float alt_scale = sum_xl / sum_l2;
+      if (this_min > 0.0f) {
+        this_min = 0.0f;
+        this_scale = alt_scale;
+      }
+      Pw8 pc;
+#pragma unroll
+      for (int i = 0; i < N; i++) {
+        float d = this_scale * lf[i] + this_min - x[i];
+        d = MAD ? fabsf(d) : d * d;
+        pc.addi(i, w[i] * d);
+      }
+      const float cur = pc.total();
+      if (cur < best) {
+        best = cur;
+        scale = this_scale;
+        b_isc = isc;
+        b_mn = mn;
+        b_fin = true;
+        mn = this_min;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++)
+    Lf[i] = (dead || !b_fin) ? 0.0f : nint_clip_f(b_isc * (x[i] - b_mn), 0, nmax);
+  o_scale = dead ? 0.0f : scale;
+  o_negmin = -mn;
+}
+
+// Index of the first maximum of |x| (np.argmax: first NaN wins).
+template <int N>
+__device__ __forceinline__ int argmax_abs(const float (&x)[N]) {
+  int idx = 0;
+  float best = fabsf(x[0]);
+  bool nan_seen = best != best;
+#pragma unroll
+  for (int i = 1; i < N; i++) {
+    const float v = fabsf(x[i]);
+    const bool take = !nan_seen && ((v != v) || v > best);
+    idx = take ? i : idx;
+    best = take ? v : best;
+    nan_seen = nan_seen || (v != v);
+  }
+  return idx;
+}
+
+template <int N>
+__device__ __forceinline__ float select_idx(const float (&x)[N], int idx) {
+  float v = x[0];
+#pragma unroll
+  for (int i = 1; i < N; i++) v = (i == idx) ? x[i] : v;
+  return v;
+}
+
+// make_qx_quants with rmse_type 1 (kquant.py:97-133): symmetric scale search over 19
+// candidates.  w holds the weights (the caller passes x*x when the reference uses qw=None).
+// Returns the scale; L receives the codes as floats offset by +nmax.
+template <int N>
+__device__ __forceinline__ float fit_qx(const float (&x)[N], const float (&w)[N], int nmax, float (&L)[N]) {
+  const int idx = argmax_abs(x);
+  const float xm = select_idx(x, idx);
+  const float amax = fabsf(xm);
+  const bool dead = amax < kGroupEps;
+  const float mx = dead ? 1.0f : xm;
+  float wx[N];
+#pragma unroll
+  for (int i = 0; i < N; i++) wx[i] = w[i] * x[i];
+  const float iscale = -(float)nmax / mx;
+  float sumlx, suml2;
+  {
+    Pw8 a, b;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float lf = nint_clip_f(iscale * x[i], -nmax, nmax - 1);
+      a.addi(i, wx[i] * lf);
+      b.addi(i, w[i] * lf * lf);
+    }
+    sumlx = a.total();
+    suml2 = b.total();
+  }
+  float scale = (suml2 != 0.0f) ? sumlx / suml2 : 0.0f;
+  float best = scale * sumlx;
+  float b_isc = iscale;
+#pragma unroll 1
+  for (int s = -9; s <= 9; s++) {
+    if (s == 0) continue;
+    const float isc = -((float)nmax + 0.1f * (float)s) / mx;
+    Pw8 a, b;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float lf = nint_clip_f(isc * x[i], -nmax, nmax - 1);
+      a.addi(i, wx[i] * lf);
+      b.addi(i, w[i] * lf * lf);
+    }
+    const float slx = a.total(), sl2 = b.total();
+    if (sl2 > 0.0f && slx * slx > best * sl2 && !dead) {
+      const float ns = slx / sl2;
+      scale = ns;
+      best = ns * slx;
+      b_isc = isc;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++)
+    L[i] = dead ? (float)nmax : nint_clip_f(b_isc * x[i], -nmax, nmax - 1) + (float)nmax;
+  return dead ? 0.0f : scale;
+}
+
+// make_q3_quants (kquant.py:136-179), Q3_K reference path: w = x*x, up to 5 sweeps of
+// per-element coordinate descent.  Codes returned offset by +nmax.
+template <int N>
+__device__ __forceinline__ float fit_q3(const float (&x)[N], int nmax, float (&Lout)[N]) {
+  const int idx = argmax_abs(x);
+  const float xm = select_idx(x, idx);
+  const bool dead = fabsf(xm) < kGroupEps;
+  const float mx = dead ? 1.0f : xm;
+  const float iscale = -(float)nmax / mx;
+  float L[N], w[N];
+  Pw8 a, b;
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    L[i] = nint_clip_f(iscale * x[i], -nmax, nmax - 1);
+    w[i] = x[i] * x[i];
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    a.addi(i, w[i] * x[i] * L[i]);
+    b.addi(i, w[i] * L[i] * L[i]);
+  }
+  float sumlx = a.total(), suml2 = b.total();
+  bool active = !dead;
+#pragma unroll 1
+  for (int it = 0; it < 5 && active; it++) {
+    bool changed = false;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float wi = w[i], xi = x[i], Li = L[i];
+      const float slx = sumlx - wi * xi * Li;
+      const float sl2 = suml2 - wi * Li * Li;
+      const float den = (slx == 0.0f) ? 1.0f : slx;
+      const float nl = nint_clip_f(xi * sl2 / den, -nmax, nmax - 1);
+      const float slx2 = slx + wi * xi * nl;
+      const float sl22 = sl2 + wi * nl * nl;
+      const bool acc = slx > 0.0f && nl != Li && sl22 > 0.0f && slx2 * slx2 * suml2 > sumlx * sumlx * sl22;
+      L[i] = acc ? nl : Li;
+      sumlx = acc ? slx2 : sumlx;
+      suml2 = acc ? sl22 : suml2;
+      changed = changed || acc;
+    }
+    active = changed;
+  }
+  float scale = (suml2 > 0.0f) ? sumlx / suml2 : 0.0f;
+#pragma unroll
+  for (int i = 0; i < N; i++) Lout[i] = (dead ? 0.0f : L[i]) + (float)nmax;
+  return dead ? 0.0f : scale;
+}
+
+// make_qp_quants (kquant.py:182-235): non-negative super-scale quantisation with 1 + 8
+// candidates and up to 5 coordinate-descent sweeps.  N is 16 or 8.  Codes are returned as
+// the bytes numpy's astype(uint8) gives (values wrap through int32).
+template <int N>
+__device__ __forceinline__ float fit_qp(const float (&x)[N], const float (&w)[N], int nmax, uint8_t (&Lout)[N]) {
+  float mx = x[0];
+#pragma unroll
+  for (int i = 1; i < N; i++) mx = np_max_step(mx, x[i]);
+  const bool dead = mx < kGroupEps;
+  const float mxs = dead ? 1.0f : mx;
+  float iscale = (float)nmax / mxs;
+  float best_mse;
+  {
+    const float scale = 1.0f / iscale;
+    Pw8 p;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float l0 = (float)nint(iscale * x[i]);
+      const float d = x[i] - scale * l0;
+      p.addi(i, w[i] * d * d);
+    }
+    best_mse = p.total();
+  }
+#pragma unroll 1
+  for (int s = -4; s <= 4; s++) {
+    if (s == 0) continue;
+    const float isc = (0.1f * (float)s + (float)nmax) / mxs;
+    const float sc = 1.0f / isc;
+    Pw8 p;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float l = (float)min(nint(isc * x[i]), nmax);
+      const float d = x[i] - sc * l;
+      p.addi(i, w[i] * d * d);
+    }
+    const float mse = p.total();
+    if (mse < best_mse && !dead) {
+      best_mse = mse;
+      iscale = isc;
+    }
+  }
+  float L[N];
+  Pw8 a, b;
+#pragma unroll
+  for (int i = 0; i < N; i++) L[i] = (float)min(nint(iscale * x[i]), nmax);
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    a.addi(i, w[i] * x[i] * L[i]);
+    b.addi(i, w[i] * L[i] * L[i]);
+  }
+  float sumlx = a.total(), suml2 = b.total();
+  bool active = !dead;
+#pragma unroll 1
+  for (int it = 0; it < 5 && active; it++) {
+    bool changed = false;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float wi = w[i], xi = x[i], Li = L[i];
+      const float slx = sumlx - wi * xi * Li;
+      const float sl2 = suml2 - wi * Li * Li;
+      const float den = (slx == 0.0f) ? 1.0f : slx;
+      const float nl = (float)min(nint(xi * sl2 / den), nmax);
+      const float slx2 = slx + wi * xi * nl;
+      const float sl22 = sl2 + wi * nl * nl;
+      const bool acc = slx > 0.0f && sl2 > 0.0f && nl != Li && slx2 * slx2 * suml2 > sumlx * sumlx * sl22;
+      L[i] = acc ? nl : Li;
+      sumlx = acc ? slx2 : sumlx;
+      suml2 = acc ? sl22 : suml2;
+      changed = changed || acc;
+    }
+    active = changed;
+  }
+  float d = (suml2 > 0.0f) ? sumlx / suml2 : 0.0f;
+#pragma unroll
+  for (int i = 0; i < N; i++) Lout[i] = dead ? (uint8_t)0 : (uint8_t)(int32_t)L[i];
+  return dead ? 0.0f : d;
+}
+
+}  // namespace cpk

@@ -1,0 +1,235 @@
+// Container decoders (coldpress/kquant.py:416-727), committed-grid extraction
+// (coldpress/ef.py:87-127) and code re-packing (coldpress/ef.py:130-176).
+// One thread per superblock element; bandwidth-bound, each superblock's header is read by
+// the 256 threads that decode it (served from L1).
+#include <cuda_runtime.h>
+#include "kq_common.cuh"
+#include "kquant_kernels.h"
+
+namespace cpk {
+
+bool grid_spec(int type, int* sbw, int* lo, int* hi, bool* has_min) {
+  switch (type) {
+    case kQ2_K: *sbw = 16; *lo = 0; *hi = 3; *has_min = true; return true;
+    case kQ3_K: *sbw = 16; *lo = -4; *hi = 3; *has_min = false; return true;
+    case kQ4_K: *sbw = 32; *lo = 0; *hi = 15; *has_min = true; return true;
+    case kQ5_K: *sbw = 32; *lo = 0; *hi = 31; *has_min = true; return true;
+    case kQ6_K: *sbw = 16; *lo = -32; *hi = 31; *has_min = false; return true;
+    default: return false;
+  }
+}
+
+__device__ __forceinline__ uint16_t ld16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// Signed code (ef.py's L) of element i of superblock b.
+template <int T>
+__device__ __forceinline__ int code_of(const uint8_t* b, int i) {
+  if (T == kQ2_K) {
+    const int h = i >> 7, k = (i >> 5) & 3, l = i & 31;
+    return (b[16 + h * 32 + l] >> (2 * k)) & 3;
+  } else if (T == kQ3_K) {
+    const int h = i >> 7, k = (i >> 5) & 3, l = i & 31;
+    const int lo = (b[32 + h * 32 + l] >> (2 * k)) & 3;
+    const int hb = (b[i & 31] >> (i >> 5)) & 1;
+    return lo - (hb ? 0 : 4);
+  } else if (T == kQ4_K || T == kQ5_K) {
+    const int c = i >> 6, r = i & 63, l = r & 31;
+    const int off = (T == kQ5_K) ? 48 : 16;
+    int v = (r < 32) ? (b[off + c * 32 + l] & 0xF) : (b[off + c * 32 + l] >> 4);
+    if (T == kQ5_K) v += 16 * ((b[16 + l] >> (2 * c + (r >= 32 ? 1 : 0))) & 1);
+    return v;
+  } else {  // Q6_K
+    const int h = i >> 7, r = i & 127, k = r >> 5, l = r & 31;
+    const uint8_t* ql = b + h * 64;
+    const uint8_t* qh = b + 128 + h * 32;
+    int lo4 = (k == 0) ? (ql[l] & 0xF) : (k == 1) ? (ql[32 + l] & 0xF) : (k == 2) ? (ql[l] >> 4) : (ql[32 + l] >> 4);
+    return (lo4 | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+  }
+}
+
+// (dl, ml) of sub-block j of superblock b (ml = 0 for types without a min).
+template <int T>
+__device__ __forceinline__ void grid_of(const uint8_t* b, int j, float& dl, float& ml) {
+  if (T == kQ2_K) {
+    dl = f16tof32(ld16(b + 80)) * (float)(b[j] & 0xF);
+    ml = f16tof32(ld16(b + 82)) * (float)(b[j] >> 4);
+  } else if (T == kQ3_K) {
+    const int lo = (j < 8) ? (b[96 + j] & 0xF) : (b[96 + j - 8] >> 4);
+    const int hi = (b[96 + 8 + (j & 3)] >> (2 * (j >> 2))) & 3;
+    dl = f16tof32(ld16(b + 108)) * (float)((lo | (hi << 4)) - 32);
+    ml = 0.0f;
+  } else if (T == kQ4_K || T == kQ5_K) {
+    const uint8_t* sc = b + 4;
+    int s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    dl = f16tof32(ld16(b)) * (float)s;
+    ml = f16tof32(ld16(b + 2)) * (float)m;
+  } else {
+    dl = f16tof32(ld16(b + 208)) * (float)(int8_t)b[192 + j];
+    ml = 0.0f;
+  }
+}
+
+template <int T>
+__global__ void dequant_kernel(const uint8_t* __restrict__ raw, int64_t nsb, float* __restrict__ out) {
+  const int64_t sb = blockIdx.x;
+  const int i = threadIdx.x;
+  if (sb >= nsb) return;
+  constexpr int BB = block_bytes(T);
+  constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
+  const uint8_t* b = raw + sb * BB;
+  float dl, ml;
+  grid_of<T>(b, i / SW, dl, ml);
+  const float v = dl * (float)code_of<T>(b, i);
+  out[sb * 256 + i] = (T == kQ3_K || T == kQ6_K) ? v : v - ml;
+}
+
+__global__ void dequant_q80_kernel(const uint8_t* __restrict__ raw, int64_t nblk, float* __restrict__ out) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nblk * 32) return;
+  const uint8_t* b = raw + (e >> 5) * 34;
+  out[e] = f16tof32(ld16(b)) * (float)(int8_t)b[2 + (e & 31)];
+}
+
+template <int T>
+__global__ void grid_kernel(const uint8_t* __restrict__ raw, int64_t nsub_total, float* __restrict__ dl,
+                            float* __restrict__ ml) {
+  constexpr int NS = (T == kQ4_K || T == kQ5_K) ? 8 : 16;
+  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= nsub_total) return;
+  float a, m;
+  grid_of<T>(raw + (s / NS) * block_bytes(T), (int)(s % NS), a, m);
+  dl[s] = a;
+  if (ml) ml[s] = m;
+}
+
+template <int T>
+__global__ void codes_kernel(const uint8_t* __restrict__ raw, int64_t nsb, int8_t* __restrict__ codes) {
+  const int64_t sb = blockIdx.x;
+  if (sb >= nsb) return;
+  codes[sb * 256 + threadIdx.x] = (int8_t)code_of<T>(raw + sb * block_bytes(T), threadIdx.x);
+}
+
+// Write signed codes into committed bytes; one thread per output code byte.
+template <int T>
+__global__ void repack_kernel(uint8_t* __restrict__ raw, const int8_t* __restrict__ codes, int64_t nsb) {
+  const int64_t sb = blockIdx.x;
+  if (sb >= nsb) return;
+  constexpr int BB = block_bytes(T);
+  __shared__ int8_t c[256];
+  c[threadIdx.x] = codes[sb * 256 + threadIdx.x];
+  __syncthreads();
+  uint8_t* b = raw + sb * BB;
+  const int t = threadIdx.x;
+  if (T == kQ2_K) {
+    if (t < 64) {
+      const int h = t >> 5, l = t & 31;
+      const int8_t* s = c + h * 128 + l;
+      b[16 + t] = (uint8_t)((s[0] & 3) | ((s[32] & 3) << 2) | ((s[64] & 3) << 4) | ((s[96] & 3) << 6));
+    }
+  } else if (T == kQ3_K) {
+    auto L = [&](int i) { return (int)c[i] + 4; };
+    if (t < 32) {
+      uint8_t m = 0;
+      for (int j = 0; j < 8; j++) m |= (uint8_t)((L(32 * j + t) > 3 ? 1 : 0) << j);
+      b[t] = m;
+    } else if (t < 96) {
+      const int q = t - 32, h = q >> 5, l = q & 31;
+      uint8_t v = 0;
+      for (int k = 0; k < 4; k++) {
+        int x = L(h * 128 + 32 * k + l);
+        x = x > 3 ? x - 4 : x;
+        v |= (uint8_t)((x & 3) << (2 * k));
+      }
+      b[32 + q] = v;
+    }
+  } else if (T == kQ4_K || T == kQ5_K) {
+    const int off = (T == kQ5_K) ? 48 : 16;
+    if (t < 128) {
+      const int cc = t >> 5, l = t & 31;
+      int lo = c[cc * 64 + l], hi = c[cc * 64 + 32 + l];
+      if (T == kQ5_K) {
+        lo = lo > 15 ? lo - 16 : lo;
+        hi = hi > 15 ? hi - 16 : hi;
+      }
+      b[off + t] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+    } else if (T == kQ5_K && t < 160) {
+      const int l = t - 128;
+      uint8_t m = 0;
+      for (int cc = 0; cc < 4; cc++) {
+        m |= (uint8_t)((c[cc * 64 + l] > 15 ? 1 : 0) << (2 * cc));
+        m |= (uint8_t)((c[cc * 64 + 32 + l] > 15 ? 1 : 0) << (2 * cc + 1));
+      }
+      b[16 + l] = m;
+    }
+  } else {  // Q6_K, codes -32..31 -> 0..63
+    auto L = [&](int i) { return (int)c[i] + 32; };
+    if (t < 128) {
+      const int h = t >> 6, r = t & 63, l = r & 31;
+      const int base = h * 128 + l;
+      b[t] = (r < 32) ? (uint8_t)((L(base) & 0xF) | ((L(base + 64) & 0xF) << 4))
+                      : (uint8_t)((L(base + 32) & 0xF) | ((L(base + 96) & 0xF) << 4));
+    } else if (t < 192) {
+      const int q = t - 128, h = q >> 5, l = q & 31;
+      const int base = h * 128 + l;
+      b[128 + q] = (uint8_t)((L(base) >> 4) | ((L(base + 32) >> 4) << 2) | ((L(base + 64) >> 4) << 4) |
+                             ((L(base + 96) >> 4) << 6));
+    }
+  }
+}
+
+#define CPK_DISPATCH_K(type, KERNEL_CALL) \
+  switch (type) {                         \
+    case kQ2_K: { constexpr int T = kQ2_K; KERNEL_CALL; } break; \
+    case kQ3_K: { constexpr int T = kQ3_K; KERNEL_CALL; } break; \
+    case kQ4_K: { constexpr int T = kQ4_K; KERNEL_CALL; } break; \
+    case kQ5_K: { constexpr int T = kQ5_K; KERNEL_CALL; } break; \
+    case kQ6_K: { constexpr int T = kQ6_K; KERNEL_CALL; } break; \
+    default: return 1;                    \
+  }
+
+int launch_dequantize(int type, const uint8_t* raw, int64_t nrow, int64_t n, float* out, cudaStream_t stream) {
+  if (type == kQ8_0) {
+    const int64_t nblk = nrow * (n / 32);
+    if (nblk) dequant_q80_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, stream>>>(raw, nblk, out);
+    return 0;
+  }
+  const int64_t nsb = nrow * (n / 256);
+  if (nsb == 0) return 0;
+  CPK_DISPATCH_K(type, (dequant_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, nsb, out)));
+  return 0;
+}
+
+int launch_grid_params(int type, const uint8_t* raw, int64_t nrow, int64_t n, float* dl, float* ml,
+                       cudaStream_t stream) {
+  int sbw, lo, hi;
+  bool hm;
+  if (!grid_spec(type, &sbw, &lo, &hi, &hm)) return 1;
+  const int64_t ns = nrow * (n / sbw);
+  if (ns == 0) return 0;
+  const unsigned g = (unsigned)((ns + 255) / 256);
+  CPK_DISPATCH_K(type, (grid_kernel<T><<<g, 256, 0, stream>>>(raw, ns, dl, ml)));
+  return 0;
+}
+
+int launch_codes(int type, const uint8_t* raw, int64_t nrow, int64_t n, int8_t* codes, cudaStream_t stream) {
+  const int64_t nsb = nrow * (n / 256);
+  if (nsb == 0) return 0;
+  CPK_DISPATCH_K(type, (codes_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, nsb, codes)));
+  return 0;
+}
+
+int launch_repack(int type, uint8_t* raw, const int8_t* codes, int64_t nrow, int64_t n, cudaStream_t stream) {
+  const int64_t nsb = nrow * (n / 256);
+  if (nsb == 0) return 0;
+  CPK_DISPATCH_K(type, (repack_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, codes, nsb)));
+  return 0;
+}
+
+}  // namespace cpk

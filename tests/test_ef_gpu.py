@@ -1,0 +1,117 @@
+"""CUDA error-feedback encoder vs the reference.
+
+Gates (north star): >= 99.9 % of integer codes identical and Hessian-weighted error within
+0.1 % of ef.py in fp32.  The ordered sweep is designed to be byte-identical, so the tests
+also report (and on the golden fixtures require) exact bytes."""
+import numpy as np
+import pytest
+
+from conftest import K_TYPES, h_weighted_err
+
+pytestmark = pytest.mark.gpu
+CODE_GATE = 0.999
+HERR_GATE = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ef():
+    from perm_b200 import ef as ef_mod
+    return ef_mod
+
+
+def _codes_equal_frac(orc, tt, a, b, nrow, n):
+    return float(np.mean(orc.codes(tt, a, nrow, n) == orc.codes(tt, b, nrow, n)))
+
+
+def test_factor_matches_reference(ef, ef_golden, factor_golden):
+    H = ef_golden["H"].astype(np.float64)
+    order = ef_golden["order"]
+    U = ef.cholesky_inv_upper(H[np.ix_(order, order)], 0.01).astype(np.float32)
+    iu = np.triu_indices(H.shape[0])
+    want = ef_golden["U_upper"]
+    rel = np.abs(U[iu] - want) / np.maximum(np.abs(want), 1e-30)
+    assert np.mean(U[iu] == want) > 0.999, f"{np.mean(U[iu] != want) * 100:.3f}% of f32 entries differ"
+    assert rel.max() < 1e-6
+    assert np.allclose(np.tril(U, -1), 0)
+    Upd = ef.cholesky_inv_upper(factor_golden["H_pd"], damp=0.01)
+    assert np.allclose(Upd, factor_golden["U_pd"], rtol=1e-11, atol=1e-14)
+
+
+def test_factor_escalates_damp_on_non_pd(ef, factor_golden, capsys):
+    U = ef.cholesky_inv_upper(factor_golden["H_bad"], damp=0.01)
+    assert np.all(np.isfinite(U)) and np.allclose(U, np.triu(U))
+    assert np.allclose(U, factor_golden["U_bad"], rtol=1e-9, atol=1e-13)
+    assert "damp escalated" in capsys.readouterr().err
+
+
+def test_factor_degenerate_raises(ef):
+    H = -np.eye(128)
+    with pytest.raises(np.linalg.LinAlgError):
+        ef.cholesky_inv_upper(H, damp=0.01, _max_tries=2)
+
+
+@pytest.mark.parametrize("qmode", ["imat", "ref"])
+@pytest.mark.parametrize("tt", K_TYPES)
+def test_ef_matches_reference_golden(ef, orc, ef_golden, tt, qmode):
+    W = ef_golden[f"W/{tt}"]
+    H = ef_golden["H"].astype(np.float64)
+    qw = ef_golden["qw"] if qmode == "imat" else None
+    raw, recon = ef.ef_encode(W, tt, qw, H, n_iter=2, act_order=True)
+    want = ef_golden[f"raw/{qmode}/{tt}"]
+    nrow, n = W.shape
+    frac = _codes_equal_frac(orc, tt, raw, want, nrow, n)
+    e_got = h_weighted_err(W, recon, H)
+    e_ref = h_weighted_err(W, ef_golden[f"recon/{qmode}/{tt}"], H)
+    assert frac >= CODE_GATE, f"codes identical {frac * 100:.4f}%"
+    assert abs(e_got / e_ref - 1) <= HERR_GATE
+    assert np.array_equal(raw, want), f"{np.count_nonzero(raw != want)} bytes differ (codes {frac * 100:.4f}%)"
+
+
+@pytest.mark.parametrize("tt", K_TYPES)
+def test_ef_single_iteration_and_storage_order(ef, ef_golden, tt):
+    W = ef_golden[f"W/{tt}"]
+    H = ef_golden["H"].astype(np.float64)
+    qw = ef_golden["qw"]
+    raw1, _ = ef.ef_encode(W, tt, qw, H, n_iter=1, act_order=True)
+    assert np.array_equal(raw1, ef_golden[f"raw1/imat/{tt}"])
+    raws, _ = ef.ef_encode(W, tt, qw, H, n_iter=2, act_order=False)
+    assert np.array_equal(raws, ef_golden[f"raw_storage/imat/{tt}"])
+
+
+def _config0(seed=12345):
+    """W 3072x1024 N(0, 0.02) with 1% outlier columns x8; H = X^T X / n,
+    X 8192x1024 N(0,1) times log-normal(0,1) channel scales; qw = diag(H)."""
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((3072, 1024)) * 0.02).astype(np.float32)
+    W[:, rng.choice(1024, 10, replace=False)] *= 8
+    sc = rng.lognormal(0, 1, 1024).astype(np.float32)
+    X = rng.standard_normal((8192, 1024)).astype(np.float32) * sc
+    H = (X.T.astype(np.float64) @ X.astype(np.float64)) / 8192
+    return W, H, np.diag(H).astype(np.float32)
+
+
+def test_ef_config0_matches_oracle(ef, orc):
+    W, H, qw = _config0()
+    raw, recon = ef.ef_encode(W, "Q2_K", qw, H, n_iter=2, act_order=True)
+    oraw, orecon = orc.ef_encode(W, "Q2_K", qw, H, n_iter=2, act_order=True)
+    frac = _codes_equal_frac(orc, "Q2_K", raw, oraw, *W.shape)
+    rel = h_weighted_err(W, recon, H) / h_weighted_err(W, orecon, H) - 1
+    assert frac >= CODE_GATE, f"codes identical {frac * 100:.4f}%"
+    assert abs(rel) <= HERR_GATE, f"H-weighted error differs by {rel * 100:.4f}%"
+    print(f"config0 EF: codes identical {frac * 100:.4f}%, bytes identical "
+          f"{np.mean(raw == oraw) * 100:.4f}%, H-err rel {rel * 100:+.5f}%")
+
+
+@pytest.mark.parametrize("tt", ["Q3_K", "Q6_K", "Q4_K"])
+def test_ef_wide_input_matches_oracle(ef, orc, tt):
+    rng = np.random.default_rng(77)
+    n, nrow = 2048, 96
+    W = (rng.standard_normal((nrow, n)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((4096, n)).astype(np.float32) * rng.lognormal(0, 1, n).astype(np.float32)
+    H = (X.T.astype(np.float64) @ X.astype(np.float64)) / 4096
+    qw = np.diag(H).astype(np.float32)
+    raw, recon = ef.ef_encode(W, tt, qw, H)
+    oraw, orecon = orc.ef_encode(W, tt, qw, H)
+    frac = _codes_equal_frac(orc, tt, raw, oraw, nrow, n)
+    rel = h_weighted_err(W, recon, H) / h_weighted_err(W, orecon, H) - 1
+    assert frac >= CODE_GATE and abs(rel) <= HERR_GATE, (frac, rel)
