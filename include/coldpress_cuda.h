@@ -40,6 +40,16 @@ extern "C" {
 int cp_version(void);
 const char* cp_last_error(void);
 
+/* Per-kernel-class device timing for benchmarks.  While enabled, every launch made by this
+ * thread through the calls below is bracketed by CUDA events on its stream.
+ * cp_profile_collect waits for them and returns, per class (0 k-quant fit, 1 error-feedback
+ * sweep, 2 factorisation, 3 other), the summed milliseconds and the number of calls, then
+ * clears the record.  Either output pointer may be NULL (host arrays of 4). */
+void cp_profile_enable(int on);
+/* Kernels launched by this library since it was loaded (all threads). */
+int64_t cp_launch_count(void);
+int cp_profile_collect(double* ms, int64_t* launches);
+
 /* Bytes of one packed block of `ggml_type` (kquant.py:21 BYTES_PER_SB; 34 for Q8_0), or 0. */
 int cp_block_bytes(int ggml_type);
 
@@ -67,6 +77,16 @@ int cp_kquant_codes(int ggml_type, const uint8_t* raw, int64_t nrow, int64_t n, 
 int cp_kquant_repack(int ggml_type, uint8_t* raw, const int8_t* codes, int64_t nrow, int64_t n,
                      void* stream);
 
+/* ef.py:298-301 encode_gguf statistics: *out (device float64) = sum over the tensor of
+ * (DEQUANTIZE(raw) - x)^2 * w[column], with w == NULL meaning 1 (the reference's weights are
+ * qw or ones).  Accumulated in float64 (the reference sums in float32; this is a diagnostic). */
+int cp_weighted_err(int ggml_type, const uint8_t* raw, const float* x, const float* w, int64_t nrow, int64_t n,
+                    double* out, void* stream);
+
+/* hessians.py:542-560 load_hessian arithmetic: H (float64 [d, d]) = float64(h16) * hscale with
+ * the exact float32 diagonal diag32 (may be NULL) written over it; h16 holds float16 bits. */
+int cp_hessian_decode(const uint16_t* h16, const float* diag32, double hscale, int64_t d, double* H, void* stream);
+
 /* ef.py:46-84 cholesky_inv_upper with ef.py:187-189 folded in: for the act-order permutation
  * `order` (int32 [n]), U_out = float32(chol(inv(H[order][:,order] + diag_shift*I)).T), upper
  * triangular [n, n].  diag_shift is the reference's damp*mean(diag(H[order][:,order])) + 1e-8.
@@ -80,26 +100,30 @@ int cp_factor_u(const double* H, int64_t n, const int32_t* order, double diag_sh
 int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double diag_shift, double* U_out,
                     void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
 
-/* ef.py:179-218 ef_encode given U (the float32 factor above) and the act-order permutation:
- * n_iter rounds of {commit grid with QUANTIZE(w_cur, qw); ordered column sweep; repack}.
- * out: packed bytes as cp_kquant_encode.  first_fit_out (optional, may be NULL) receives the
- * first round's committed bytes, which equal QUANTIZE(x, qw) (encode_gguf's stock baseline,
- * ef.py:298).  workspace >= cp_ef_workspace_bytes(type, nrow, n). */
+/* Device layout of U for the sweep: a column-pair-interleaved transpose plus the diagonal,
+ * cp_ef_u_bytes(n) bytes.  Built once per factor (q/k/v and gate/up share theirs). */
+size_t cp_ef_u_bytes(int64_t n);
+int cp_ef_prepare_u(const float* U, int64_t n, float* u_prepared, void* stream);
+
+/* ef.py:179-218 ef_encode given the prepared factor of H[order][:, order] and the act-order
+ * permutation `order` (int32 [n]): n_iter rounds of {commit grid with QUANTIZE(w_cur, qw);
+ * ordered column sweep; repack}.  out: packed bytes as cp_kquant_encode.  first_fit_out
+ * (optional, may be NULL) receives the first round's committed bytes, which equal
+ * QUANTIZE(x, qw), encode_gguf's stock baseline (ef.py:298).
+ * workspace >= cp_ef_workspace_bytes(type, nrow, n). */
 size_t cp_ef_workspace_bytes(int ggml_type, int64_t nrow, int64_t n);
 int cp_ef_encode(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
-                 const float* U, const float* qw, int n_iter, uint8_t* out, uint8_t* first_fit_out,
+                 const float* u_prepared, const float* qw, int n_iter, uint8_t* out, uint8_t* first_fit_out,
                  void* workspace, size_t workspace_bytes, void* stream);
 
-/* One error-feedback pass (ef.py:197-216) against committed grid (dl, ml from
+/* One error-feedback pass (ef.py:197-216) against a committed grid (dl, ml from
  * cp_grid_params): codes int8 [nrow, n] in storage order; w_out (optional) receives the
- * compensated weights un-permuted (ef.py:215-216).  UT2 and diagU come from
- * cp_ef_prepare_u.  workspace >= cp_ef_sweep_workspace_bytes(nrow, n). */
-size_t cp_ef_u_bytes(int64_t n);
-int cp_ef_prepare_u(const float* U, int64_t n, float* ut2_and_diag, void* stream);
+ * compensated weights un-permuted (ef.py:215-216), the next round's fit input.
+ * workspace >= cp_ef_sweep_workspace_bytes(nrow, n). */
 size_t cp_ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
 int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
-                const float* U, const float* ut2_and_diag, const float* dl, const float* ml,
-                int8_t* codes, float* w_out, void* workspace, size_t workspace_bytes, void* stream);
+                const float* u_prepared, const float* dl, const float* ml, int8_t* codes, float* w_out,
+                void* workspace, size_t workspace_bytes, void* stream);
 
 /* hessians.py:455-470 hook arithmetic: H += x^T x for x bf16 [T, d] (row-major, d a
  * multiple of 128), H float32 [d, d], accumulated in float32 on the tensor cores. */

@@ -42,18 +42,23 @@ def lib():
         "cp_version": ([], I),
         "cp_last_error": ([], ctypes.c_char_p),
         "cp_block_bytes": ([I], I),
+        "cp_profile_enable": ([I], None),
+        "cp_launch_count": ([], I64),
+        "cp_profile_collect": ([P, P], I),
         "cp_kquant_encode": ([I, P, I64, I64, P, P, P], I),
         "cp_kquant_decode": ([I, P, I64, I64, P, P], I),
         "cp_grid_params": ([I, P, I64, I64, P, P, P], I),
         "cp_kquant_codes": ([I, P, I64, I64, P, P], I),
         "cp_kquant_repack": ([I, P, P, I64, I64, P], I),
+        "cp_weighted_err": ([I, P, P, P, I64, I64, P, P], I),
+        "cp_hessian_decode": ([P, P, D, I64, P, P], I),
         "cp_factor_workspace_bytes": ([I64], SZ),
         "cp_factor_u": ([P, I64, P, D, P, P, SZ, P, P], I),
         "cp_factor_u_f64": ([P, I64, P, D, P, P, SZ, P, P], I),
         "cp_ef_u_bytes": ([I64], SZ),
         "cp_ef_prepare_u": ([P, I64, P, P], I),
         "cp_ef_sweep_workspace_bytes": ([I64, I64], SZ),
-        "cp_ef_sweep": ([I, P, I64, I64, P, P, P, P, P, P, P, P, SZ, P], I),
+        "cp_ef_sweep": ([I, P, I64, I64, P, P, P, P, P, P, P, SZ, P], I),
         "cp_ef_workspace_bytes": ([I, I64, I64], SZ),
         "cp_ef_encode": ([I, P, I64, I64, P, P, P, I, P, P, P, SZ, P], I),
         "cp_xtx_accumulate": ([P, I64, I64, P, P], I),
@@ -64,6 +69,22 @@ def lib():
         f.restype = res
     _lib = L
     return L
+
+
+PROFILE_CLASSES = ("fit", "sweep", "factor", "other")
+
+
+def profile_enable(on=True):
+    lib().cp_profile_enable(1 if on else 0)
+
+
+def profile_collect():
+    """{class: (ms, launches)} of the launches recorded since the last collect."""
+    ms = (ctypes.c_double * 4)()
+    cnt = (ctypes.c_int64 * 4)()
+    check(lib().cp_profile_collect(ctypes.cast(ms, ctypes.c_void_p), ctypes.cast(cnt, ctypes.c_void_p)),
+          "profile_collect")
+    return {c: (ms[i], cnt[i]) for i, c in enumerate(PROFILE_CLASSES)}
 
 
 def last_error():

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <cstdio>
 #include <cstring>
+#include <vector>
 #include "../../include/coldpress_cuda.h"
 #include "ef_kernels.h"
 #include "kq_common.cuh"
@@ -47,8 +48,49 @@ int check_shape(int t, int64_t nrow, int64_t n, bool allow_q80) {
 
 size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
+// Optional per-kernel-class timing: when enabled, each launch below is bracketed by two CUDA
+// events recorded on its stream; cp_profile_collect sums the elapsed times per class.
+// Host-thread-local and not thread-safe, like the rest of the calling convention.
+enum ProfClass { kProfFit = 0, kProfSweep = 1, kProfFactor = 2, kProfOther = 3, kProfClasses = 4 };
+struct ProfMark {
+  int cls;
+  cudaEvent_t a, b;
+};
+thread_local bool g_prof = false;
+thread_local std::vector<ProfMark> g_marks;
+thread_local std::vector<cudaEvent_t> g_free_events;
+
+cudaEvent_t prof_event() {
+  if (!g_free_events.empty()) {
+    cudaEvent_t e = g_free_events.back();
+    g_free_events.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct ProfScope {
+  bool on;
+  ProfMark m;
+  cudaStream_t s;
+  ProfScope(int cls, cudaStream_t stream) : on(g_prof), s(stream) {
+    if (!on) return;
+    m.cls = cls;
+    m.a = prof_event();
+    m.b = prof_event();
+    cudaEventRecord(m.a, s);
+  }
+  ~ProfScope() {
+    if (!on) return;
+    cudaEventRecord(m.b, s);
+    g_marks.push_back(m);
+  }
+};
+
 struct EfLayout {
-  size_t ut2, sweep, wcur, dl, ml, codes, total;
+  size_t sweep, wcur, dl, ml, codes, total;
 };
 
 EfLayout ef_layout(int t, int64_t nrow, int64_t n) {
@@ -57,7 +99,6 @@ EfLayout ef_layout(int t, int64_t nrow, int64_t n) {
   cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
   EfLayout L;
   size_t off = 0;
-  L.ut2 = off; off += align256(cpk::ef_ut2_bytes(n));
   L.sweep = off; off += align256(cpk::ef_sweep_workspace_bytes(nrow, n));
   L.wcur = off; off += align256((size_t)nrow * n * sizeof(float));
   L.dl = off; off += align256((size_t)nrow * (n / sbw) * sizeof(float));
@@ -73,6 +114,31 @@ extern "C" {
 
 int cp_version(void) { return 100; }
 
+void cp_profile_enable(int on) { g_prof = on != 0; }
+
+int64_t cp_launch_count(void) { return cpk::g_launches.load(); }
+
+int cp_profile_collect(double* ms, int64_t* launches) {
+  for (int c = 0; c < kProfClasses; c++) {
+    if (ms) ms[c] = 0.0;
+    if (launches) launches[c] = 0;
+  }
+  int rc = CP_OK;
+  for (const ProfMark& m : g_marks) {
+    float t = 0.0f;
+    if (cudaEventSynchronize(m.b) != cudaSuccess || cudaEventElapsedTime(&t, m.a, m.b) != cudaSuccess) {
+      rc = check_launch("cp_profile_collect");
+    } else {
+      if (ms) ms[m.cls] += t;
+      if (launches) launches[m.cls] += 1;
+    }
+    g_free_events.push_back(m.a);
+    g_free_events.push_back(m.b);
+  }
+  g_marks.clear();
+  return rc;
+}
+
 const char* cp_last_error(void) { return g_err; }
 
 int cp_block_bytes(int ggml_type) { return cpk::block_bytes(ggml_type); }
@@ -82,6 +148,7 @@ int cp_kquant_encode(int t, const float* x, int64_t nrow, int64_t n, const float
   if ((!x || !out) && nrow > 0) return set_err(CP_ERR_ARG, "null pointer");
   if (((uintptr_t)x | (uintptr_t)qw) & 15) return set_err(CP_ERR_ARG, "x and qw must be 16-byte aligned");
   if (t != cpk::kQ8_0 && ((uintptr_t)out & 15)) return set_err(CP_ERR_ARG, "out must be 16-byte aligned");
+  ProfScope ps(kProfFit, (cudaStream_t)stream);
   return check_rc(cpk::launch_quantize(t, x, nrow, n, qw, out, (cudaStream_t)stream), "cp_kquant_encode");
 }
 
@@ -109,6 +176,20 @@ int cp_kquant_repack(int t, uint8_t* raw, const int8_t* codes, int64_t nrow, int
   return check_rc(cpk::launch_repack(t, raw, codes, nrow, n, (cudaStream_t)stream), "cp_kquant_repack");
 }
 
+int cp_weighted_err(int t, const uint8_t* raw, const float* x, const float* w, int64_t nrow, int64_t n, double* out,
+                    void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if (!out || ((!raw || !x) && nrow > 0)) return set_err(CP_ERR_ARG, "null pointer");
+  return check_rc(cpk::launch_weighted_err(t, raw, x, w, nrow, n, out, (cudaStream_t)stream), "cp_weighted_err");
+}
+
+int cp_hessian_decode(const uint16_t* h16, const float* diag32, double hscale, int64_t d, double* H, void* stream) {
+  if (d <= 0 || d > 65536) return set_err(CP_ERR_SHAPE, "d out of range");
+  if (!h16 || !H) return set_err(CP_ERR_ARG, "null pointer");
+  ProfScope ps(kProfOther, (cudaStream_t)stream);
+  return check_rc(cpk::launch_hessian_decode(h16, diag32, hscale, d, H, (cudaStream_t)stream), "cp_hessian_decode");
+}
+
 size_t cp_factor_workspace_bytes(int64_t n) { return n > 0 ? cpk::factor_workspace_bytes(n) : 0; }
 
 static int factor_common(const double* H, int64_t n, const int32_t* order, double diag_shift, void* U_out,
@@ -117,6 +198,7 @@ static int factor_common(const double* H, int64_t n, const int32_t* order, doubl
   if (n > 65536) return set_err(CP_ERR_SHAPE, "n too large");
   if (!H || !order || !U_out || !workspace || !status_dev) return set_err(CP_ERR_ARG, "null pointer");
   if (ws_bytes < cpk::factor_workspace_bytes(n)) return set_err(CP_ERR_WORKSPACE, "factor workspace too small");
+  ProfScope ps(kProfFactor, (cudaStream_t)stream);
   return check_rc(cpk::launch_factor_u(H, n, order, diag_shift, U_out, f64, workspace, status_dev,
                                        (cudaStream_t)stream),
                   "cp_factor_u");
@@ -145,7 +227,7 @@ size_t cp_ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
   return (nrow > 0 && n > 0) ? cpk::ef_sweep_workspace_bytes(nrow, n) : 0;
 }
 
-int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* U,
+int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order,
                 const float* ut2, const float* dl, const float* ml, int8_t* codes, float* w_out, void* workspace,
                 size_t ws_bytes, void* stream) {
   if (int rc = check_shape(t, nrow, n, false)) return rc;
@@ -153,9 +235,10 @@ int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* o
   int sbw, lo, hi;
   bool hm;
   cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
-  if (!x || !order || !U || !ut2 || !dl || (hm && !ml) || !codes || !workspace) return set_err(CP_ERR_ARG, "null pointer");
+  if (!x || !order || !ut2 || !dl || (hm && !ml) || !codes || !workspace) return set_err(CP_ERR_ARG, "null pointer");
   if (ws_bytes < cpk::ef_sweep_workspace_bytes(nrow, n)) return set_err(CP_ERR_WORKSPACE, "sweep workspace too small");
-  return check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, U, ut2, ut2 + (size_t)n * n, dl, ml, workspace, codes,
+  ProfScope ps(kProfSweep, (cudaStream_t)stream);
+  return check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, ut2 + (size_t)n * n, dl, ml, workspace, codes,
                                        w_out, (cudaStream_t)stream),
                   "cp_ef_sweep");
 }
@@ -165,39 +248,43 @@ size_t cp_ef_workspace_bytes(int t, int64_t nrow, int64_t n) {
   return ef_layout(t, nrow, n).total;
 }
 
-int cp_ef_encode(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* U, const float* qw,
+int cp_ef_encode(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* ut2, const float* qw,
                  int n_iter, uint8_t* out, uint8_t* first_fit_out, void* workspace, size_t ws_bytes, void* stream) {
   if (int rc = check_shape(t, nrow, n, false)) return rc;
   if (nrow == 0) return CP_OK;
   if (n_iter < 1 || n_iter > 64) return set_err(CP_ERR_ARG, "n_iter must be in 1..64");
-  if (!x || !order || !U || !out || !workspace) return set_err(CP_ERR_ARG, "null pointer");
+  if (!x || !order || !ut2 || !out || !workspace) return set_err(CP_ERR_ARG, "null pointer");
   if (((uintptr_t)x | (uintptr_t)qw | (uintptr_t)out | (uintptr_t)workspace) & 15)
     return set_err(CP_ERR_ARG, "x, qw, out and workspace must be 16-byte aligned");
   const EfLayout L = ef_layout(t, nrow, n);
   if (ws_bytes < L.total) return set_err(CP_ERR_WORKSPACE, "ef workspace too small");
   cudaStream_t s = (cudaStream_t)stream;
   char* ws = (char*)workspace;
-  float* ut2 = (float*)(ws + L.ut2);
   float* wcur = (float*)(ws + L.wcur);
   float* dl = (float*)(ws + L.dl);
   float* ml = (float*)(ws + L.ml);
   int8_t* codes = (int8_t*)(ws + L.codes);
   int rc;
-  if ((rc = check_rc(cpk::launch_build_ut2(U, n, ut2, ut2 + (size_t)n * n, s), "cp_ef_encode: U layout"))) return rc;
   for (int it = 0; it < n_iter; it++) {
     // commit the grid from the current (compensated) weights; round 1 starts from x
     const float* src = it == 0 ? x : wcur;
-    if ((rc = check_rc(cpk::launch_quantize(t, src, nrow, n, qw, out, s), "cp_ef_encode: fit"))) return rc;
+    {
+      ProfScope ps(kProfFit, s);
+      if ((rc = check_rc(cpk::launch_quantize(t, src, nrow, n, qw, out, s), "cp_ef_encode: fit"))) return rc;
+    }
     if (it == 0 && first_fit_out) {
       const size_t nb = (size_t)nrow * (n / 256) * cpk::block_bytes(t);
       if (cudaMemcpyAsync(first_fit_out, out, nb, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
         return check_launch("cp_ef_encode: first-fit copy");
     }
     if ((rc = check_rc(cpk::launch_grid_params(t, out, nrow, n, dl, ml, s), "cp_ef_encode: grid"))) return rc;
-    if ((rc = check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, U, ut2, ut2 + (size_t)n * n, dl, ml, ws + L.sweep,
-                                            codes, it + 1 < n_iter ? wcur : nullptr, s),
-                       "cp_ef_encode: sweep")))
-      return rc;
+    {
+      ProfScope ps(kProfSweep, s);
+      if ((rc = check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, ut2 + (size_t)n * n, dl, ml, ws + L.sweep,
+                                              codes, it + 1 < n_iter ? wcur : nullptr, s),
+                         "cp_ef_encode: sweep")))
+        return rc;
+    }
     if ((rc = check_rc(cpk::launch_repack(t, out, codes, nrow, n, s), "cp_ef_encode: repack"))) return rc;
   }
   return CP_OK;

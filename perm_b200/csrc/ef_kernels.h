@@ -8,7 +8,7 @@ namespace cpk {
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
 size_t ef_ut2_bytes(int64_t n);
 int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream);
-int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* U,
+int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order,
                     const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
                     int8_t* codes, float* wcur, cudaStream_t stream);
 size_t factor_workspace_bytes(int64_t n);

@@ -62,7 +62,7 @@ __global__ void build_ut2_kernel(const float* __restrict__ U, int n, float* __re
 template <bool HAS_MIN>
 __global__ void __launch_bounds__(256, 2)
 ef_sweep_kernel(const float* __restrict__ x, int nrow, int n, const int* __restrict__ order,
-                const float* __restrict__ U, const float* __restrict__ UT2, const float* __restrict__ diagU,
+                const float* __restrict__ UT2, const float* __restrict__ diagU,
                 const float* __restrict__ dl, const float* __restrict__ ml, int sbw, int lo, int hi,
                 float2* __restrict__ work, int8_t* __restrict__ codes, float* __restrict__ wcur, float nz) {
   __shared__ float s_u[32][33];
@@ -88,9 +88,9 @@ ef_sweep_kernel(const float* __restrict__ x, int nrow, int n, const int* __restr
   __syncthreads();
 
   for (int j0 = 0; j0 < n; j0 += 32) {
-    for (int i = threadIdx.x; i < 32 * 32; i += 256) {
-      const int a = i >> 5, b = i & 31;
-      s_u[a][b] = __ldg(U + (size_t)(j0 + a) * n + j0 + b);
+    for (int i = threadIdx.x; i < 32 * 32; i += 256) {  // s_u[a][b] = U[j0+a][j0+b]
+      const int a = i & 31, b = i >> 5;
+      s_u[a][b] = __ldg(UT2 + ((size_t)((j0 + b) >> 1) * n + j0 + a) * 2 + (b & 1));
     }
     if (threadIdx.x < 32) s_ord[threadIdx.x] = __ldg(order + j0 + threadIdx.x);
     __syncthreads();
@@ -161,10 +161,11 @@ int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaSt
   if (n % 32) return 2;
   dim3 grid((unsigned)(n / 32), (unsigned)(n / 32));
   build_ut2_kernel<<<grid, 256, 0, stream>>>(U, (int)n, UT2, diagU);
+  note_launch();
   return 0;
 }
 
-int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* U,
+int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order,
                     const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
                     int8_t* codes, float* wcur, cudaStream_t stream) {
   int sbw, lo, hi;
@@ -173,11 +174,12 @@ int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int
   if (n % 256 || nrow <= 0) return 2;
   const unsigned ntiles = (unsigned)((nrow + 31) / 32);
   if (has_min)
-    ef_sweep_kernel<true><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, U, UT2, diagU, dl, ml, sbw, lo,
+    ef_sweep_kernel<true><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, UT2, diagU, dl, ml, sbw, lo,
                                                      hi, (float2*)work, codes, wcur, -0.0f);
   else
-    ef_sweep_kernel<false><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, U, UT2, diagU, dl, nullptr,
+    ef_sweep_kernel<false><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, UT2, diagU, dl, nullptr,
                                                       sbw, lo, hi, (float2*)work, codes, wcur, -0.0f);
+  note_launch();
   return 0;
 }
 

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "ef_kernels.h"
+#include "kquant_kernels.h"
 
 namespace cpk {
 
@@ -268,28 +269,38 @@ int launch_factor_u(const double* H, int64_t n64, const int* order, double shift
   {
     dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
     permute_reverse_kernel<<<g, 256, 0, stream>>>(H, n, order, shift, P);
+    note_launch();
   }
   for (int k = 0; k < n; k += NB) {
     potrf_diag_kernel<<<1, 256, 0, stream>>>(P, n, k, Dinv, status);
+    note_launch();
     const int rem = n - k - NB;
     if (rem > 0) {
       const int tiles = (rem + 63) / 64;
       trsm_panel_kernel<<<tiles, 256, 0, stream>>>(P, n, k, Dinv, status);
+      note_launch();
       syrk_kernel<<<tiles * (tiles + 1) / 2, 256, 0, stream>>>(P, n, k, status);
+      note_launch();
     }
   }
   // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower)
   for (int j = n - NB; j >= 0; j -= NB) {
     trti2_kernel<<<1, 64, 0, stream>>>(P, n, j, Dinv, status);
+    note_launch();
     const int rem = n - j - NB;
     const int tiles = (rem + 63) / 64;
-    if (rem > 0) trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+    if (rem > 0) {
+      trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+      note_launch();
+    }
     trinv_apply_kernel<<<tiles + 1, 256, 0, stream>>>(P, n, j, T, Dinv, status);
+    note_launch();
   }
   {
     dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
     if (out_f64) unreverse_cast_kernel<double><<<g, 256, 0, stream>>>(P, n, (double*)U);
     else unreverse_cast_kernel<float><<<g, 256, 0, stream>>>(P, n, (float*)U);
+    note_launch();
   }
   return 0;
 }

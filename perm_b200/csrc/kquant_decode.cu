@@ -184,6 +184,37 @@ __global__ void repack_kernel(uint8_t* __restrict__ raw, const int8_t* __restric
   }
 }
 
+// encode_gguf statistics (ef.py:298-301): sum over the tensor of (dequant(raw) - x)^2 * w[col]
+// (w == nullptr means 1), accumulated in float64.  One CTA per superblock group.
+template <int T>
+__global__ void __launch_bounds__(256) weighted_err_kernel(const uint8_t* __restrict__ raw, const float* __restrict__ x,
+                                                           const float* __restrict__ w, int64_t nsb, int64_t nsb_row,
+                                                           double* __restrict__ out) {
+  constexpr int BB = block_bytes(T);
+  constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
+  double acc = 0.0;
+  for (int64_t sb = blockIdx.x; sb < nsb; sb += gridDim.x) {
+    const uint8_t* b = raw + sb * BB;
+    const int i = threadIdx.x;
+    float dl, ml;
+    grid_of<T>(b, i / SW, dl, ml);
+    float v = dl * (float)code_of<T>(b, i);
+    if (!(T == kQ3_K || T == kQ6_K)) v = v - ml;
+    const float d = v - x[sb * 256 + i];
+    const float wt = w ? w[(sb % nsb_row) * 256 + i] : 1.0f;
+    acc += (double)(d * d * wt);
+  }
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ double red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int k = 0; k < 8; k++) s += red[k];
+    atomicAdd(out, s);
+  }
+}
+
 #define CPK_DISPATCH_K(type, KERNEL_CALL) \
   switch (type) {                         \
     case kQ2_K: { constexpr int T = kQ2_K; KERNEL_CALL; } break; \
@@ -197,12 +228,16 @@ __global__ void repack_kernel(uint8_t* __restrict__ raw, const int8_t* __restric
 int launch_dequantize(int type, const uint8_t* raw, int64_t nrow, int64_t n, float* out, cudaStream_t stream) {
   if (type == kQ8_0) {
     const int64_t nblk = nrow * (n / 32);
-    if (nblk) dequant_q80_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, stream>>>(raw, nblk, out);
+    if (nblk) {
+      dequant_q80_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, stream>>>(raw, nblk, out);
+      note_launch();
+    }
     return 0;
   }
   const int64_t nsb = nrow * (n / 256);
   if (nsb == 0) return 0;
   CPK_DISPATCH_K(type, (dequant_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, nsb, out)));
+  note_launch();
   return 0;
 }
 
@@ -215,6 +250,7 @@ int launch_grid_params(int type, const uint8_t* raw, int64_t nrow, int64_t n, fl
   if (ns == 0) return 0;
   const unsigned g = (unsigned)((ns + 255) / 256);
   CPK_DISPATCH_K(type, (grid_kernel<T><<<g, 256, 0, stream>>>(raw, ns, dl, ml)));
+  note_launch();
   return 0;
 }
 
@@ -222,6 +258,7 @@ int launch_codes(int type, const uint8_t* raw, int64_t nrow, int64_t n, int8_t* 
   const int64_t nsb = nrow * (n / 256);
   if (nsb == 0) return 0;
   CPK_DISPATCH_K(type, (codes_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, nsb, codes)));
+  note_launch();
   return 0;
 }
 
@@ -229,6 +266,39 @@ int launch_repack(int type, uint8_t* raw, const int8_t* codes, int64_t nrow, int
   const int64_t nsb = nrow * (n / 256);
   if (nsb == 0) return 0;
   CPK_DISPATCH_K(type, (repack_kernel<T><<<(unsigned)nsb, 256, 0, stream>>>(raw, codes, nsb)));
+  note_launch();
+  return 0;
+}
+
+// hessians.py:542-560 load_hessian: H = float64(H16) * hscale, then the exact float32
+// diagonal written over it (diag32 may be null for the old float32-only layout).
+__global__ void hessian_decode_kernel(const uint16_t* __restrict__ h16, const float* __restrict__ diag32, double hscale,
+                                      int64_t d, double* __restrict__ H) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= d * d) return;
+  const int64_t r = i / d, c = i - r * d;
+  double v = (double)__half2float(__ushort_as_half(h16[i])) * hscale;
+  if (r == c && diag32) v = (double)diag32[r];
+  H[i] = v;
+}
+
+int launch_hessian_decode(const uint16_t* h16, const float* diag32, double hscale, int64_t d, double* H,
+                          cudaStream_t stream) {
+  const int64_t n = d * d;
+  if (n == 0) return 0;
+  hessian_decode_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(h16, diag32, hscale, d, H);
+  note_launch();
+  return 0;
+}
+
+int launch_weighted_err(int type, const uint8_t* raw, const float* x, const float* w, int64_t nrow, int64_t n,
+                        double* out, cudaStream_t stream) {
+  const int64_t nsb = nrow * (n / 256);
+  if (cudaMemsetAsync(out, 0, sizeof(double), stream) != cudaSuccess) return 3;
+  if (nsb == 0) return 0;
+  const unsigned g = (unsigned)(nsb < 4096 ? nsb : 4096);
+  CPK_DISPATCH_K(type, (weighted_err_kernel<T><<<g, 256, 0, stream>>>(raw, x, w, nsb, n / 256, out)));
+  note_launch();
   return 0;
 }
 

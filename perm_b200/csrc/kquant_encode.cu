@@ -608,6 +608,7 @@ int launch_quantize(int type, const float* x, int64_t nrow, int64_t n, const flo
     const int64_t nblk = nrow * (n / 32);
     if (nblk == 0) return 0;
     q80_encode_kernel<<<(unsigned)((nblk + 127) / 128), 128, 0, stream>>>(x, nblk, out);
+    note_launch();
     return 0;
   }
   const int64_t nsb_row = n / 256, total = nrow * nsb_row;
@@ -638,6 +639,7 @@ int launch_quantize(int type, const float* x, int64_t nrow, int64_t n, const flo
     default:
       return 1;
   }
+  note_launch();
   return 0;
 }
 

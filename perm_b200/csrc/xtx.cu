@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include "xtx_kernels.h"
+#include "kquant_kernels.h"
 
 namespace cpk {
 
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(256) xtx_simt_kernel(const __nv_bfloat16* __re
 int launch_xtx(const uint16_t* x, int64_t T, int64_t d, float* H, cudaStream_t stream) {
   const int tiles = (int)(d / 64);
   xtx_simt_kernel<<<tiles * (tiles + 1) / 2, 256, 0, stream>>>((const __nv_bfloat16*)x, T, (int)d, H);
+  note_launch();
   return 0;
 }
 

@@ -83,9 +83,19 @@ def cholesky_inv_upper(H, damp=0.01, _max_tries=6):
     return np.ascontiguousarray(U.cpu().numpy())
 
 
-def ef_encode_dev(x_dev, ttype, qw_dev, U_dev, order, n_iter=2, stream=None, want_first_fit=False,
-                  workspace=None):
-    """Device EF given the float32 factor U of H[order][:, order].  Returns (raw, first_fit)."""
+def prepare_u_dev(U_dev, stream=None):
+    """Sweep layout of the float32 factor (built once per distinct Hessian)."""
+    torch = nat.torch_cuda()
+    n = int(U_dev.shape[0])
+    L = nat.lib()
+    ut2 = torch.empty(L.cp_ef_u_bytes(n) // 4, dtype=torch.float32, device=U_dev.device)
+    nat.check(L.cp_ef_prepare_u(nat.ptr(U_dev), n, nat.ptr(ut2), nat.stream_ptr(torch, stream)), "prepare_u")
+    return ut2
+
+
+def ef_encode_dev(x_dev, ttype, qw_dev, ut2_dev, order, n_iter=2, stream=None, want_first_fit=False,
+                  workspace=None, out=None):
+    """Device EF given the prepared factor of H[order][:, order].  Returns (raw, first_fit)."""
     torch = nat.torch_cuda()
     if ttype not in nat.K_TYPES:
         raise ValueError(ttype)
@@ -98,11 +108,12 @@ def ef_encode_dev(x_dev, ttype, qw_dev, U_dev, order, n_iter=2, stream=None, wan
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=x_dev.device)
     order_dev = order if isinstance(order, torch.Tensor) else \
         torch.from_numpy(np.asarray(order, np.int32)).to(x_dev.device)
-    raw = torch.empty((nrow, kq.row_bytes(ttype, n)), dtype=torch.uint8, device=x_dev.device)
+    raw = out if out is not None else \
+        torch.empty((nrow, kq.row_bytes(ttype, n)), dtype=torch.uint8, device=x_dev.device)
     first = torch.empty_like(raw) if want_first_fit else None
-    nat.check(L.cp_ef_encode(TYPE_ID[ttype], nat.ptr(x_dev), nrow, n, nat.ptr(order_dev), nat.ptr(U_dev),
+    nat.check(L.cp_ef_encode(TYPE_ID[ttype], nat.ptr(x_dev), nrow, n, nat.ptr(order_dev), nat.ptr(ut2_dev),
                              nat.ptr(qw_dev), int(n_iter), nat.ptr(raw), nat.ptr(first), nat.ptr(workspace),
-                             ws_bytes, nat.stream_ptr(torch, stream)), f"ef_encode[{ttype}]")
+                             workspace.numel(), nat.stream_ptr(torch, stream)), f"ef_encode[{ttype}]")
     return raw, first
 
 
@@ -121,6 +132,6 @@ def ef_encode(x, ttype, qw, H, n_iter=2, damp=0.01, act_order=True):
     x_dev = torch.from_numpy(np.ascontiguousarray(x, dtype=F32)).cuda()
     qw_dev = None if qw is None else torch.from_numpy(
         np.ascontiguousarray(np.broadcast_to(np.asarray(qw, F32), (n,)))).cuda()
-    raw, _ = ef_encode_dev(x_dev, ttype, qw_dev, U_dev, order, n_iter)
+    raw, _ = ef_encode_dev(x_dev, ttype, qw_dev, prepare_u_dev(U_dev), order, n_iter)
     recon = kq.dequantize_dev(ttype, raw, n)
     return raw.cpu().numpy(), recon.cpu().numpy()

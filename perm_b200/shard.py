@@ -1,0 +1,131 @@
+"""Sharding of a whole-model encode across the GPUs of one node.
+
+Work units are (tensor, row range): error-feedback rows are independent once U and the
+per-row committed grid are known, and k-quant superblocks never straddle rows, so a tensor
+can be split at any row boundary and its packed rows concatenated afterwards.  There is no
+exchange during compute; the only collective is the gather of packed bytes (and the per-unit
+error sums of the statistics) to rank 0.
+
+Cost model (per unit, arbitrary but consistent units):
+    EF:    sweep 2 * n_iter * rows * n^2/2 ordered updates + n_iter fits
+    fit:   rows * n * passes(type, path), passes = candidate evaluations per element
+    factor (2/3) n^3 FP64 flops, charged once per distinct Hessian per rank
+Greedy LPT: units sorted by cost, each to the rank whose load (including any factorisation
+it would newly need) grows least.  Units of one Hessian group are kept whole unless they
+exceed a fair share, so U is usually computed once per node.
+"""
+from dataclasses import dataclass, field
+
+# candidate evaluations per element of one fit (kquant.py: 1 + nstep+1 candidates for qkx,
+# 19 for make_qx, ~6 for the Q3_K reference path), imatrix / reference path
+FIT_PASSES = {("Q2_K", True): 38, ("Q2_K", False): 17, ("Q3_K", True): 19, ("Q3_K", False): 6,
+              ("Q4_K", True): 38, ("Q4_K", False): 22, ("Q5_K", True): 38, ("Q5_K", False): 17,
+              ("Q6_K", True): 19, ("Q6_K", False): 19}
+FIT_OP_WEIGHT = 10.0      # ops per candidate-element relative to one ordered update
+FACTOR_WEIGHT = 4.0       # FP64 flop relative to one ordered update
+
+
+@dataclass
+class UnitMeta:
+    name: str
+    ttype: str
+    mode: str
+    nrow: int
+    n: int
+    hkey: str = None
+    imat: bool = True
+
+
+@dataclass
+class Unit:
+    name: str
+    r0: int
+    r1: int
+    cost: float
+
+
+@dataclass
+class Plan:
+    world: int
+    units: list = field(default_factory=list)        # per rank: list of Unit
+    loads: list = field(default_factory=list)
+
+    def rank_units(self, r):
+        return self.units[r]
+
+
+def unit_cost(m, rows, n_iter=2):
+    fit = rows * m.n * FIT_PASSES.get((m.ttype, m.imat), 20) * FIT_OP_WEIGHT
+    if m.mode == "EF":
+        return n_iter * (rows * m.n * (m.n - 1) / 2.0) + n_iter * fit
+    if m.mode == "wRTN(attn0-diag)":
+        return 2 * fit
+    return fit
+
+
+def factor_cost(n):
+    return FACTOR_WEIGHT * (2.0 / 3.0) * float(n) ** 3
+
+
+def make_plan(metas, world, n_iter=2, split_factor=2.0):
+    """Split and assign units.  metas: list of UnitMeta.  Returns Plan."""
+    plan = Plan(world, [[] for _ in range(world)], [0.0] * world)
+    if world == 1:
+        for m in metas:
+            plan.units[0].append(Unit(m.name, 0, m.nrow, unit_cost(m, m.nrow, n_iter)))
+        plan.loads[0] = sum(u.cost for u in plan.units[0])
+        return plan
+    total = sum(unit_cost(m, m.nrow, n_iter) for m in metas)
+    fair = total / world
+    cap = fair / split_factor
+    groups = {}
+    for m in metas:
+        groups.setdefault(m.hkey if m.mode == "EF" else ("solo", m.name), []).append(m)
+    items = []   # (cost, hkey or None, [(meta, r0, r1)])
+    for key, ms in groups.items():
+        gcost = sum(unit_cost(m, m.nrow, n_iter) for m in ms)
+        hk = key if not isinstance(key, tuple) else None
+        if gcost <= cap:
+            items.append((gcost, hk, [(m, 0, m.nrow) for m in ms]))
+            continue
+        for m in ms:
+            c = unit_cost(m, m.nrow, n_iter)
+            pieces = max(1, int(-(-c // cap)))
+            step = -(-m.nrow // pieces)
+            for r0 in range(0, m.nrow, step):
+                r1 = min(m.nrow, r0 + step)
+                items.append((unit_cost(m, r1 - r0, n_iter), hk, [(m, r0, r1)]))
+    items.sort(key=lambda t: -t[0])
+    have = [set() for _ in range(world)]
+    dims = {m.hkey: m.n for m in metas if m.hkey is not None}
+    for cost, hk, parts in items:
+        best, best_load = 0, None
+        for r in range(world):
+            extra = factor_cost(dims[hk]) if (hk is not None and hk not in have[r]) else 0.0
+            load = plan.loads[r] + cost + extra
+            if best_load is None or load < best_load:
+                best, best_load = r, load
+        plan.loads[best] = best_load
+        if hk is not None:
+            have[best].add(hk)
+        for m, r0, r1 in parts:
+            plan.units[best].append(Unit(m.name, r0, r1, unit_cost(m, r1 - r0, n_iter)))
+    return plan
+
+
+def gather_to_rank0(torch, dist, flat, sizes, rank, world):
+    """Send each rank's flat uint8 buffer to rank 0 over NCCL; returns the list of received
+    buffers on rank 0 (rank 0's own buffer first) and None elsewhere."""
+    if world == 1:
+        return [flat]
+    if rank == 0:
+        bufs = [flat] + [torch.empty(int(sizes[r]), dtype=torch.uint8, device=flat.device) for r in range(1, world)]
+        ops = [dist.P2POp(dist.irecv, bufs[r], r) for r in range(1, world) if sizes[r] > 0]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        return bufs
+    if sizes[rank] > 0:
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, flat, 0)]):
+            req.wait()
+    return None
