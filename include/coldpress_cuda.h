@@ -125,6 +125,51 @@ int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const in
                 const float* u_prepared, const float* dl, const float* ml, int8_t* codes, float* w_out,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- grouped calls
+ * The same operations over many tensors in as few launches as possible (one per ~256 jobs),
+ * so a whole model fills the GPU even where single tensors are small.  Job arrays live in
+ * host memory and may be discarded when the call returns. */
+
+typedef struct {
+  const float* x;   /* [nrow, n] */
+  const float* qw;  /* [n] imatrix means, or NULL for the reference path */
+  uint8_t* out;     /* [nrow, n/256 * cp_block_bytes(type)] */
+  int64_t nrow, n;
+} cp_fit_job;
+/* kquant.py:732 QUANTIZE for every job (all of one k-quant type). */
+int cp_kquant_encode_batch(int ggml_type, const cp_fit_job* jobs, int count, void* stream);
+
+typedef struct {
+  int ggml_type;
+  const uint8_t* raw;   /* committed bytes (grid params, weighted error) */
+  uint8_t* raw_out;     /* bytes to re-pack (repack) */
+  const int8_t* codes;  /* [nrow, n] (repack) */
+  const float* x;       /* [nrow, n] (weighted error) */
+  const float* w;       /* [n] or NULL (weighted error) */
+  float* dl;            /* grid params outputs, as cp_grid_params */
+  float* ml;
+  double* err;          /* weighted error: the call ADDS this tensor's sum to *err */
+  int64_t nrow, n;
+} cp_block_job;
+int cp_grid_params_batch(const cp_block_job* jobs, int count, void* stream);   /* ef.py:87-127 */
+int cp_kquant_repack_batch(const cp_block_job* jobs, int count, void* stream); /* ef.py:130-176 */
+int cp_weighted_err_batch(const cp_block_job* jobs, int count, void* stream);  /* ef.py:298-301 */
+
+typedef struct {
+  int ggml_type;
+  const float* x;
+  int64_t nrow, n;
+  const int32_t* order;
+  const float* u_prepared;
+  const float* dl;
+  const float* ml;      /* NULL for Q3_K / Q6_K */
+  int8_t* codes;
+  float* w_out;         /* optional */
+  void* workspace;      /* cp_ef_sweep_workspace_bytes(nrow, n) bytes, one per job */
+} cp_sweep_job;
+/* ef.py:197-216 for every job in one launch (a CTA per 32 rows of any job). */
+int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream);
+
 /* hessians.py:455-470 hook arithmetic: H += x^T x for x bf16 [T, d] (row-major, d a
  * multiple of 128), H float32 [d, d], accumulated in float32 on the tensor cores. */
 int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream);

@@ -22,6 +22,32 @@ GRID = {"Q2_K": (16, 0, 3, True), "Q3_K": (16, -4, 3, False), "Q4_K": (32, 0, 15
         "Q5_K": (32, 0, 31, True), "Q6_K": (16, -32, 31, False)}
 
 
+class FitJob(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("qw", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("nrow", ctypes.c_int64), ("n", ctypes.c_int64)]
+
+
+class BlockJob(ctypes.Structure):
+    _fields_ = [("ggml_type", ctypes.c_int), ("raw", ctypes.c_void_p), ("raw_out", ctypes.c_void_p),
+                ("codes", ctypes.c_void_p), ("x", ctypes.c_void_p), ("w", ctypes.c_void_p),
+                ("dl", ctypes.c_void_p), ("ml", ctypes.c_void_p), ("err", ctypes.c_void_p),
+                ("nrow", ctypes.c_int64), ("n", ctypes.c_int64)]
+
+
+class SweepJob(ctypes.Structure):
+    _fields_ = [("ggml_type", ctypes.c_int), ("x", ctypes.c_void_p), ("nrow", ctypes.c_int64),
+                ("n", ctypes.c_int64), ("order", ctypes.c_void_p), ("u_prepared", ctypes.c_void_p),
+                ("dl", ctypes.c_void_p), ("ml", ctypes.c_void_p), ("codes", ctypes.c_void_p),
+                ("w_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p)]
+
+
+def job_array(cls, items):
+    arr = (cls * max(1, len(items)))()
+    for i, it in enumerate(items):
+        arr[i] = it
+    return arr
+
+
 class CudaPathError(RuntimeError):
     """A CUDA call of the encoder failed (launch error, bad argument, missing library)."""
 
@@ -62,6 +88,11 @@ def lib():
         "cp_ef_workspace_bytes": ([I, I64, I64], SZ),
         "cp_ef_encode": ([I, P, I64, I64, P, P, P, I, P, P, P, SZ, P], I),
         "cp_xtx_accumulate": ([P, I64, I64, P, P], I),
+        "cp_kquant_encode_batch": ([I, P, I, P], I),
+        "cp_grid_params_batch": ([P, I, P], I),
+        "cp_kquant_repack_batch": ([P, I, P], I),
+        "cp_weighted_err_batch": ([P, I, P], I),
+        "cp_ef_sweep_batch": ([P, I, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -114,6 +145,11 @@ def torch_cuda():
 
 def ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def addr(t):
+    """Raw device address for a job struct field (None for a missing tensor)."""
+    return t.data_ptr() if t is not None else None
 
 
 def stream_ptr(torch, stream=None):

@@ -290,6 +290,131 @@ int cp_ef_encode(int t, const float* x, int64_t nrow, int64_t n, const int32_t* 
   return CP_OK;
 }
 
+// ---------------------------------------------------------------------------- grouped calls
+
+int cp_kquant_encode_batch(int t, const cp_fit_job* jobs, int count, void* stream) {
+  if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
+  if (!is_k_type(t)) return set_err(CP_ERR_TYPE, "grouped fits support the k-quant types");
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int pass = 0; pass < 2; pass++) {  // imatrix jobs, then reference-path jobs
+    static thread_local cpk::FitBatch b;
+    b.count = 0;
+    int64_t ctas = 0;
+    for (int i = 0; i <= count; i++) {
+      const bool flush = (i == count) || b.count == cpk::kFitBatchMax;
+      if (flush && b.count) {
+        ProfScope ps(kProfFit, s);
+        if (int rc = check_rc(cpk::launch_quantize_batch(t, pass == 0, b, ctas, s), "cp_kquant_encode_batch")) return rc;
+        b.count = 0;
+        ctas = 0;
+      }
+      if (i == count) break;
+      const cp_fit_job& j = jobs[i];
+      if ((j.qw != nullptr) != (pass == 0)) continue;
+      if (int rc = check_shape(t, j.nrow, j.n, false)) return rc;
+      if (j.nrow == 0) continue;
+      if (!j.x || !j.out || (((uintptr_t)j.x | (uintptr_t)j.qw | (uintptr_t)j.out) & 15))
+        return set_err(CP_ERR_ARG, "null or unaligned pointer in a fit job");
+      cpk::FitDesc& d = b.d[b.count++];
+      d.x = j.x;
+      d.qw = j.qw;
+      d.out = j.out;
+      d.nsb_row = j.n / 256;
+      d.nsb = j.nrow * d.nsb_row;
+      d.cta0 = ctas;
+      ctas += cpk::quantize_batch_ctas(t, d.nsb);
+    }
+  }
+  return CP_OK;
+}
+
+static int block_batch(int op, const cp_block_job* jobs, int count, void* stream, const char* what) {
+  if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
+  cudaStream_t s = (cudaStream_t)stream;
+  static thread_local cpk::SbBatch b;
+  b.count = 0;
+  int64_t total = 0;
+  for (int i = 0; i <= count; i++) {
+    const bool flush = (i == count) || b.count == cpk::kSbBatchMax;
+    if (flush && b.count) {
+      ProfScope ps(kProfOther, s);
+      if (int rc = check_rc(cpk::launch_sb_batch(op, b, total, s), what)) return rc;
+      b.count = 0;
+      total = 0;
+    }
+    if (i == count) break;
+    const cp_block_job& j = jobs[i];
+    if (int rc = check_shape(j.ggml_type, j.nrow, j.n, false)) return rc;
+    if (j.nrow == 0) continue;
+    const bool ok = op == 0 ? (j.raw && j.dl) : op == 1 ? (j.raw_out && j.codes) : (j.raw && j.x && j.err);
+    if (!ok) return set_err(CP_ERR_ARG, "null pointer in a block job");
+    cpk::SbDesc& d = b.d[b.count++];
+    d.raw = j.raw;
+    d.raw_w = j.raw_out;
+    d.codes = j.codes;
+    d.x = j.x;
+    d.w = j.w;
+    d.dl = j.dl;
+    d.ml = j.ml;
+    d.err = j.err;
+    d.nsb_row = j.n / 256;
+    d.nsb = j.nrow * d.nsb_row;
+    d.sb0 = total;
+    d.type = j.ggml_type;
+    total += d.nsb;
+  }
+  return CP_OK;
+}
+
+int cp_grid_params_batch(const cp_block_job* jobs, int count, void* stream) {
+  return block_batch(0, jobs, count, stream, "cp_grid_params_batch");
+}
+
+int cp_kquant_repack_batch(const cp_block_job* jobs, int count, void* stream) {
+  return block_batch(1, jobs, count, stream, "cp_kquant_repack_batch");
+}
+
+int cp_weighted_err_batch(const cp_block_job* jobs, int count, void* stream) {
+  return block_batch(2, jobs, count, stream, "cp_weighted_err_batch");
+}
+
+int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
+  if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
+  cudaStream_t s = (cudaStream_t)stream;
+  int64_t all_tiles = 0;
+  for (int i = 0; i < count; i++) all_tiles += (jobs[i].nrow + 31) / 32;
+  // one-warp CTAs only when there are enough tiles to keep ~16 resident per SM
+  const int warps = all_tiles >= 2 * 16 * 148 ? 1 : 8;
+  static thread_local cpk::SweepBatch b;
+  b.count = 0;
+  int tiles = 0;
+  for (int i = 0; i <= count; i++) {
+    const bool flush = (i == count) || b.count == cpk::kSweepBatchMax;
+    if (flush && b.count) {
+      ProfScope ps(kProfSweep, s);
+      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, warps, s), "cp_ef_sweep_batch")) return rc;
+      b.count = 0;
+      tiles = 0;
+    }
+    if (i == count) break;
+    const cp_sweep_job& j = jobs[i];
+    if (int rc = check_shape(j.ggml_type, j.nrow, j.n, false)) return rc;
+    if (j.nrow == 0) continue;
+    if (!j.x || !j.order || !j.u_prepared || !j.dl || !j.codes || !j.workspace)
+      return set_err(CP_ERR_ARG, "null pointer in a sweep job");
+    cpk::SweepDesc& d = b.d[b.count];
+    if (!cpk::sweep_desc(j.ggml_type, j.x, j.nrow, j.n, j.order, j.u_prepared, j.dl, j.ml, j.workspace, j.codes,
+                         j.w_out, &d))
+      return set_err(CP_ERR_TYPE, "cp_ef_sweep_batch: unsupported type");
+    if (d.ml == nullptr && (j.ggml_type == cpk::kQ2_K || j.ggml_type == cpk::kQ4_K || j.ggml_type == cpk::kQ5_K))
+      return set_err(CP_ERR_ARG, "ml is required for Q2_K/Q4_K/Q5_K");
+    d.tile0 = tiles;
+    tiles += (int)((j.nrow + 31) / 32);
+    b.count++;
+  }
+  return CP_OK;
+}
+
 int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream) {
   if (T < 0 || d <= 0 || d % 128) return set_err(CP_ERR_SHAPE, "d must be a positive multiple of 128");
   if (T == 0) return CP_OK;

@@ -5,6 +5,26 @@
 #include <cuda_runtime.h>
 
 namespace cpk {
+// One tensor of a grouped error-feedback sweep launch (tiles [tile0, tile0 + ceil(nrow/32))).
+struct SweepDesc {
+  const float* x;
+  const int* order;
+  const float* ut2;   // prepared U: interleaved transpose, then the diagonal
+  const float* dl;
+  const float* ml;    // null for types without a min
+  float2* work;
+  int8_t* codes;
+  float* wout;        // null in the last round
+  int nrow, n, sbw, lo, hi, tile0;
+};
+constexpr int kSweepBatchMax = 320;  // 88-byte descriptors: the table travels as a kernel parameter
+struct SweepBatch {
+  int count;
+  SweepDesc d[kSweepBatchMax];
+};
+bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* ut2,
+                const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d);
+int launch_ef_sweep_batch(const SweepBatch& b, int total_tiles, int warps, cudaStream_t stream);
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
 size_t ef_ut2_bytes(int64_t n);
 int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream);

@@ -59,25 +59,43 @@ __global__ void build_ut2_kernel(const float* __restrict__ U, int n, float* __re
   }
 }
 
-template <bool HAS_MIN>
-__global__ void __launch_bounds__(256, 2)
-ef_sweep_kernel(const float* __restrict__ x, int nrow, int n, const int* __restrict__ order,
-                const float* __restrict__ UT2, const float* __restrict__ diagU,
-                const float* __restrict__ dl, const float* __restrict__ ml, int sbw, int lo, int hi,
-                float2* __restrict__ work, int8_t* __restrict__ codes, float* __restrict__ wcur, float nz) {
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Sweep of one 32-row tile of one tensor.  WARPS warps per CTA: warp 0 runs the panels,
+// all WARPS warps share the trailing updates (WARPS = 1: one warp does everything and keeps
+// the block's errors in registers, many such CTAs per SM hide each other's panel latency;
+// WARPS = 8: for launches with few tiles).  Each warp streams the column pairs it updates
+// (the U segment and the 32 working rows, 512 bytes a pair) through a 4-stage cp.async ring
+// in shared memory, so global latency overlaps the update chains.
+template <int WARPS>
+__device__ __forceinline__ void sweep_tile(const SweepDesc& t, int tile, float nz) {
+  constexpr int ST = 4;
   __shared__ float s_u[32][33];
-  __shared__ __align__(16) float2 s_e[32][32];
+  __shared__ __align__(16) float2 s_e[WARPS == 1 ? 1 : 32][32];
   __shared__ int s_ord[32];
-  const int tile = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ __align__(16) float4 s_ring[WARPS][ST][32];
+  constexpr int NT = 32 * WARPS;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = t.n, nrow = t.nrow;
   const int row = tile * 32 + lane;
   const bool rv = row < nrow;
   const int npair = n >> 1;
+  const int sbw = t.sbw, lo = t.lo, hi = t.hi;
   const int nsub = n / sbw;
-  float2* W = work + (size_t)tile * npair * 32;
-  const float* xr = x + (size_t)row * n;
+  const int* __restrict__ order = t.order;
+  const float* __restrict__ UT2 = t.ut2;
+  const float* __restrict__ diagU = t.ut2 + (size_t)n * n;
+  float2* W = t.work + (size_t)tile * npair * 32;
+  const float* xr = t.x + (size_t)row * n;
 
   // wp = x[:, order]
-  for (int kp = warp; kp < npair; kp += 8) {
+  for (int kp = warp; kp < npair; kp += WARPS) {
     float2 v = make_float2(0.0f, 0.0f);
     if (rv) {
       v.x = __ldg(xr + __ldg(order + 2 * kp));
@@ -87,8 +105,9 @@ ef_sweep_kernel(const float* __restrict__ x, int nrow, int n, const int* __restr
   }
   __syncthreads();
 
+  float2 ee[32];
   for (int j0 = 0; j0 < n; j0 += 32) {
-    for (int i = threadIdx.x; i < 32 * 32; i += 256) {  // s_u[a][b] = U[j0+a][j0+b]
+    for (int i = threadIdx.x; i < 32 * 32; i += NT) {  // s_u[a][b] = U[j0+a][j0+b]
       const int a = i & 31, b = i >> 5;
       s_u[a][b] = __ldg(UT2 + ((size_t)((j0 + b) >> 1) * n + j0 + a) * 2 + (b & 1));
     }
@@ -96,58 +115,96 @@ ef_sweep_kernel(const float* __restrict__ x, int nrow, int n, const int* __restr
     __syncthreads();
 
     if (warp == 0) {
-      float w[32];
+      float w[32], dlv[32], mlv[32];
 #pragma unroll
       for (int a = 0; a < 16; a++) {
-        const float2 t = W[((j0 >> 1) + a) * 32 + lane];
-        w[2 * a] = t.x;
-        w[2 * a + 1] = t.y;
+        const float2 v = W[((j0 >> 1) + a) * 32 + lane];
+        w[2 * a] = v.x;
+        w[2 * a + 1] = v.y;
       }
-      const float* dlr = dl + (size_t)row * nsub;
-      const float* mlr = HAS_MIN ? ml + (size_t)row * nsub : nullptr;
+      const float* dlr = t.dl + (size_t)row * nsub;
+      const float* mlr = t.ml ? t.ml + (size_t)row * nsub : nullptr;
+#pragma unroll
+      for (int a = 0; a < 32; a++) {  // independent loads, issued ahead of the dependent chain
+        const int sidx = s_ord[a] / sbw;
+        dlv[a] = rv ? __ldg(dlr + sidx) : 0.0f;
+        mlv[a] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+      }
 #pragma unroll
       for (int a = 0; a < 32; a++) {
         const int j = s_ord[a];
-        const int s = j / sbw;
-        const float dlv = rv ? __ldg(dlr + s) : 0.0f;
-        const float mlv = (HAS_MIN && rv) ? __ldg(mlr + s) : 0.0f;
         int q = 0;
         float e = 0.0f;
-        if (dlv != 0.0f) {
-          q = clampi(nint((w[a] + mlv) / dlv), lo, hi);
-          const float recon = dlv * (float)q - mlv;
+        if (dlv[a] != 0.0f) {
+          q = clampi(nint((w[a] + mlv[a]) / dlv[a]), lo, hi);
+          const float recon = dlv[a] * (float)q - mlv[a];
           e = (w[a] - recon) / __ldg(diagU + j0 + a);
         }
         if (rv) {
-          codes[(size_t)row * n + j] = (int8_t)q;
-          if (wcur) wcur[(size_t)row * n + j] = w[a];
+          t.codes[(size_t)row * n + j] = (int8_t)q;
+          if (t.wout) t.wout[(size_t)row * n + j] = w[a];
         }
-        s_e[a][lane] = make_float2(e, e);
+        if constexpr (WARPS == 1) ee[a] = make_float2(e, e);
+        else s_e[a][lane] = make_float2(e, e);
 #pragma unroll
         for (int b = a + 1; b < 32; b++) w[b] = w[b] - e * s_u[a][b];
       }
     }
-    __syncthreads();
+    if constexpr (WARPS > 1) __syncthreads();
 
     const int kp0 = (j0 + 32) >> 1;
-    if (kp0 < npair) {
-      float2 ee[32];
+    const int first = kp0 + warp;
+    const int count = first < npair ? (npair - first + WARPS - 1) / WARPS : 0;
+    if (count > 0) {
+      if constexpr (WARPS > 1) {
 #pragma unroll
-      for (int a = 0; a < 32; a++) ee[a] = s_e[a][lane];
-      for (int kp = kp0 + warp; kp < npair; kp += 8) {
-        float2 wv = W[kp * 32 + lane];
-        const float4* up = reinterpret_cast<const float4*>(UT2 + ((size_t)kp * n + j0) * 2);
+        for (int a = 0; a < 32; a++) ee[a] = s_e[a][lane];
+      }
+      // lanes 0-15 fetch the pair's 64 U values, lanes 16-31 its 32 working-row float2s
+      auto issue = [&](int i) {
+        if (i < count) {
+          const int kp = first + i * WARPS;
+          const float4* src = lane < 16
+              ? reinterpret_cast<const float4*>(UT2 + ((size_t)kp * n + j0) * 2) + lane
+              : reinterpret_cast<const float4*>(W + (size_t)kp * 32) + (lane - 16);
+          cp_async16(&s_ring[warp][i % ST][lane], src);
+        }
+        cp_async_commit();
+      };
+#pragma unroll
+      for (int i = 0; i < ST - 1; i++) issue(i);
+      for (int i = 0; i < count; i++) {
+        issue(i + ST - 1);
+        cp_async_wait<ST - 1>();
+        __syncwarp();
+        const float4* U4 = &s_ring[warp][i % ST][0];
+        float2 wv = reinterpret_cast<const float2*>(&s_ring[warp][i % ST][16])[lane];
 #pragma unroll
         for (int a4 = 0; a4 < 16; a4++) {
-          const float4 u = __ldg(up + a4);
+          const float4 u = U4[a4];
           upd2(wv.x, wv.y, ee[2 * a4].x, ee[2 * a4].y, u.x, u.y, nz);
           upd2(wv.x, wv.y, ee[2 * a4 + 1].x, ee[2 * a4 + 1].y, u.z, u.w, nz);
         }
-        W[kp * 32 + lane] = wv;
+        W[(size_t)(first + i * WARPS) * 32 + lane] = wv;
+        __syncwarp();
       }
+      cp_async_wait<0>();
     }
     __syncthreads();
   }
+}
+
+template <int WARPS>
+__global__ void __launch_bounds__(32 * WARPS, WARPS == 1 ? 16 : 2)
+ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+  int lo = 0, hi = b.count - 1;
+  const int cta = blockIdx.x;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.d[mid].tile0 <= cta) lo = mid;
+    else hi = mid - 1;
+  }
+  sweep_tile<WARPS>(b.d[lo], cta - b.d[lo].tile0, nz);
 }
 
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
@@ -165,22 +222,46 @@ int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaSt
   return 0;
 }
 
+int launch_ef_sweep_batch(const SweepBatch& b, int total_tiles, int warps, cudaStream_t stream) {
+  if (b.count == 0 || total_tiles == 0) return 0;
+  if (warps == 1) ef_sweep_batch_kernel<1><<<total_tiles, 32, 0, stream>>>(b, -0.0f);
+  else ef_sweep_batch_kernel<8><<<total_tiles, 256, 0, stream>>>(b, -0.0f);
+  note_launch();
+  return 0;
+}
+
+bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* ut2,
+                const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d) {
+  int sbw, lo, hi;
+  bool has_min;
+  if (!grid_spec(type, &sbw, &lo, &hi, &has_min)) return false;
+  d->x = x;
+  d->order = order;
+  d->ut2 = ut2;
+  d->dl = dl;
+  d->ml = has_min ? ml : nullptr;
+  d->work = (float2*)work;
+  d->codes = codes;
+  d->wout = wcur;
+  d->nrow = (int)nrow;
+  d->n = (int)n;
+  d->sbw = sbw;
+  d->lo = lo;
+  d->hi = hi;
+  d->tile0 = 0;
+  return true;
+}
+
 int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order,
                     const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
                     int8_t* codes, float* wcur, cudaStream_t stream) {
-  int sbw, lo, hi;
-  bool has_min;
-  if (!grid_spec(type, &sbw, &lo, &hi, &has_min)) return 1;
+  (void)diagU;
   if (n % 256 || nrow <= 0) return 2;
-  const unsigned ntiles = (unsigned)((nrow + 31) / 32);
-  if (has_min)
-    ef_sweep_kernel<true><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, UT2, diagU, dl, ml, sbw, lo,
-                                                     hi, (float2*)work, codes, wcur, -0.0f);
-  else
-    ef_sweep_kernel<false><<<ntiles, 256, 0, stream>>>(x, (int)nrow, (int)n, order, UT2, diagU, dl, nullptr,
-                                                      sbw, lo, hi, (float2*)work, codes, wcur, -0.0f);
-  note_launch();
-  return 0;
+  SweepBatch b;
+  b.count = 1;
+  if (!sweep_desc(type, x, nrow, n, order, UT2, dl, ml, work, codes, wcur, &b.d[0])) return 1;
+  const int tiles = (int)((nrow + 31) / 32);
+  return launch_ef_sweep_batch(b, tiles, tiles >= 2 * 16 * 148 ? 1 : 8, stream);
 }
 
 }  // namespace cpk

@@ -31,56 +31,72 @@ __global__ void permute_reverse_kernel(const double* __restrict__ H, int n, cons
   P[(size_t)i * n + j] = v;
 }
 
-// In-place Cholesky of the nb x nb diagonal block at (k, k); also writes its inverse (lower)
-// into Dinv.  One CTA of 256 threads.  status != 0 stops the factorisation.
-__global__ void potrf_diag_kernel(double* __restrict__ A, int n, int k, double* __restrict__ Dinv,
-                                  int* __restrict__ status) {
+// Diagonal block at (k, k): Cholesky factor L11 of the (already updated) block, then its
+// inverse, written in place of the block.  One warp; lane l owns rows l and l + 32 and the
+// block lives in shared memory.  Nothing after this step needs L11 itself: the panel below is
+// solved with inv(L11) and the diagonal blocks of L^-1 are exactly these inverses.
+// A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
+__global__ void __launch_bounds__(32) potrf_inv_diag_kernel(double* __restrict__ A, int n, int k,
+                                                            int* __restrict__ status) {
   __shared__ double a[NB][NB + 1];
-  __shared__ int bad;
-  const int t = threadIdx.x;
-  const int nb = min(NB, n - k);
-  if (t == 0) bad = *status;
-  for (int i = t; i < NB * NB; i += blockDim.x) {
+  const int l = threadIdx.x;
+  if (*status) return;
+  for (int i = l; i < NB * NB; i += 32) {
     const int r = i / NB, c = i % NB;
-    a[r][c] = (r < nb && c <= r) ? A[(size_t)(k + r) * n + k + c] : (r == c ? 1.0 : 0.0);
+    a[r][c] = (c <= r) ? A[(size_t)(k + r) * n + k + c] : 0.0;
   }
-  __syncthreads();
-  if (bad) return;
-  for (int j = 0; j < nb; j++) {
-    if (t == 0) {
-      const double d = a[j][j];
-      if (!(d > 0.0)) bad = 1;  // not positive definite (or NaN)
-      else a[j][j] = sqrt(d);
+  __syncwarp();
+  const int rows[2] = {l, l + 32};
+  for (int j = 0; j < NB; j++) {
+    const double d = a[j][j];
+    if (!(d > 0.0)) {  // uniform: every lane read the same pivot
+      if (l == 0) *status = 1;
+      return;
     }
-    __syncthreads();
-    if (bad) break;
-    const double djj = a[j][j];
-    for (int r = j + 1 + t; r < nb; r += blockDim.x) a[r][j] /= djj;
-    __syncthreads();
-    for (int i = t; i < (nb - j - 1) * (nb - j - 1); i += blockDim.x) {
-      const int r = j + 1 + i / (nb - j - 1), c = j + 1 + i % (nb - j - 1);
-      if (c <= r) a[r][c] -= a[r][j] * a[c][j];
+    const double s = sqrt(d);
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int r = rows[q];
+      if (r == j) a[r][j] = s;
+      else if (r > j) a[r][j] /= s;
     }
-    __syncthreads();
-  }
-  if (bad) {
-    if (t == 0) *status = 1;
-    return;
-  }
-  // inverse of the lower-triangular block: column c solved by forward substitution
-  for (int c = t; c < NB; c += blockDim.x) {
-    double col[NB];
-    for (int r = 0; r < NB; r++) {
-      if (r < c) { col[r] = 0.0; continue; }
-      double s = (r == c) ? 1.0 : 0.0;
-      for (int l = c; l < r; l++) s -= a[r][l] * col[l];
-      col[r] = s / a[r][r];
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int r = rows[q];
+      if (r > j) {
+        const double v = a[r][j];
+        for (int c = j + 1; c <= r; c++) a[r][c] = fma(-v, a[c][j], a[r][c]);
+      }
     }
-    for (int r = 0; r < NB; r++) Dinv[r * NB + c] = col[r];
+    __syncwarp();
   }
-  for (int i = t; i < NB * NB; i += blockDim.x) {
+  // in-place inverse of the lower-triangular block, columns right to left (LAPACK dtrti2)
+  for (int j = NB - 1; j >= 0; j--) {
+    const double inv_jj = 1.0 / a[j][j];
+    double acc[2] = {0.0, 0.0};
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int i = rows[q];
+      if (i > j) {
+        double t = 0.0;
+        for (int kk = j + 1; kk <= i; kk++) t = fma(a[i][kk], a[kk][j], t);
+        acc[q] = t;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int i = rows[q];
+      if (i > j) a[i][j] = -inv_jj * acc[q];
+      else if (i == j) a[i][j] = inv_jj;
+    }
+    __syncwarp();
+  }
+  for (int i = l; i < NB * NB; i += 32) {
     const int r = i / NB, c = i % NB;
-    if (r < nb && c < nb) A[(size_t)(k + r) * n + k + c] = (c <= r) ? a[r][c] : 0.0;
+    A[(size_t)(k + r) * n + k + c] = (c <= r) ? a[r][c] : 0.0;
   }
 }
 
@@ -130,16 +146,15 @@ __device__ __forceinline__ void tile_gemm(const double* __restrict__ A, int lda,
   }
 }
 
-// Panel below the diagonal block: A21 := A21 * inv(L11)^T.
-__global__ void __launch_bounds__(256) trsm_panel_kernel(double* __restrict__ A, int n, int k,
-                                                         const double* __restrict__ Dinv, const int* status) {
+// Panel below the diagonal block: A21 := A21 * inv(L11)^T, inv(L11) read from the diagonal.
+__global__ void __launch_bounds__(256) trsm_panel_kernel(double* __restrict__ A, int n, int k, const int* status) {
   if (*status) return;
   const int r0 = k + NB + blockIdx.x * 64;
   const int m = min(64, n - r0);
   const int nb = min(NB, n - k);
   double acc[4][4];
-  // out[r][c] = sum_l A21[r][l] * Dinv[c][l]
-  tile_gemm<true>(A + (size_t)r0 * n + k, n, Dinv, NB, m, nb, nb, acc);
+  // out[r][c] = sum_l A21[r][l] * inv(L11)[c][l]
+  tile_gemm<true>(A + (size_t)r0 * n + k, n, A + (size_t)k * n + k, n, m, nb, nb, acc);
   const int t = threadIdx.x, tr = t / 16, tc = t % 16;
 #pragma unroll
   for (int i = 0; i < 4; i++)
@@ -194,24 +209,15 @@ __global__ void __launch_bounds__(256) trmm_kernel(const double* __restrict__ A,
     }
 }
 
-//   L21 := T * inv(L11)  and  L11 := inv(L11)
+//   L21 := T * inv(L11)   (inv(L11) already sits on the diagonal)
 __global__ void __launch_bounds__(256) trinv_apply_kernel(double* __restrict__ A, int n, int j,
-                                                          const double* __restrict__ T,
-                                                          const double* __restrict__ Dinv, const int* status) {
+                                                          const double* __restrict__ T, const int* status) {
   if (*status) return;
   const int base = j + NB;
-  if ((int)blockIdx.x * 64 + base >= n) {
-    // the extra CTA writes the inverted diagonal block
-    for (int i = threadIdx.x; i < NB * NB; i += blockDim.x) {
-      const int r = i / NB, c = i % NB;
-      if (j + r < n && j + c < n) A[(size_t)(j + r) * n + j + c] = Dinv[i];
-    }
-    return;
-  }
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
   double acc[4][4];
-  tile_gemm<false>(T + (size_t)(r0 - base) * NB, NB, Dinv, NB, m, NB, NB, acc);
+  tile_gemm<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, NB, NB, acc);
   const int t = threadIdx.x, tr = t / 16, tc = t % 16;
 #pragma unroll
   for (int i = 0; i < 4; i++)
@@ -220,29 +226,6 @@ __global__ void __launch_bounds__(256) trinv_apply_kernel(double* __restrict__ A
       const int r = tr + 16 * i, cc = tc + 16 * c;
       if (r < m) A[(size_t)(r0 + r) * n + j + cc] = acc[i][c];
     }
-}
-
-// Inverse of the (already factorised, lower) diagonal block at (j, j) into Dinv.
-__global__ void trti2_kernel(const double* __restrict__ A, int n, int j, double* __restrict__ Dinv,
-                             const int* status) {
-  if (*status) return;
-  __shared__ double a[NB][NB + 1];
-  const int t = threadIdx.x;
-  for (int i = t; i < NB * NB; i += blockDim.x) {
-    const int r = i / NB, c = i % NB;
-    a[r][c] = (c <= r) ? A[(size_t)(j + r) * n + j + c] : 0.0;
-  }
-  __syncthreads();
-  for (int c = t; c < NB; c += blockDim.x) {
-    double col[NB];
-    for (int r = 0; r < NB; r++) {
-      if (r < c) { col[r] = 0.0; continue; }
-      double s = (r == c) ? 1.0 : 0.0;
-      for (int l = c; l < r; l++) s -= a[r][l] * col[l];
-      col[r] = s / a[r][r];
-    }
-    for (int r = 0; r < NB; r++) Dinv[r * NB + c] = col[r];
-  }
 }
 
 // U[i][j] = Linv[n-1-i][n-1-j] for j >= i, else 0 (cast to OutT).
@@ -254,8 +237,8 @@ __global__ void unreverse_cast_kernel(const double* __restrict__ Linv, int n, Ou
 }
 
 size_t factor_workspace_bytes(int64_t n) {
-  // P (n x n f64) + Dinv (nb x nb) + T (n x nb)
-  return ((size_t)n * n + (size_t)NB * NB + (size_t)n * NB) * sizeof(double);
+  // P (n x n f64) + T (n x nb)
+  return ((size_t)n * n + (size_t)n * NB) * sizeof(double);
 }
 
 int launch_factor_u(const double* H, int64_t n64, const int* order, double shift, void* U, bool out_f64,
@@ -263,8 +246,7 @@ int launch_factor_u(const double* H, int64_t n64, const int* order, double shift
   if (n64 <= 0 || n64 % NB) return 2;
   const int n = (int)n64;
   double* P = (double*)work;
-  double* Dinv = P + (size_t)n * n;
-  double* T = Dinv + NB * NB;
+  double* T = P + (size_t)n * n;
   cudaMemsetAsync(status, 0, sizeof(int), stream);
   {
     dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
@@ -272,28 +254,25 @@ int launch_factor_u(const double* H, int64_t n64, const int* order, double shift
     note_launch();
   }
   for (int k = 0; k < n; k += NB) {
-    potrf_diag_kernel<<<1, 256, 0, stream>>>(P, n, k, Dinv, status);
+    potrf_inv_diag_kernel<<<1, 32, 0, stream>>>(P, n, k, status);
     note_launch();
     const int rem = n - k - NB;
     if (rem > 0) {
       const int tiles = (rem + 63) / 64;
-      trsm_panel_kernel<<<tiles, 256, 0, stream>>>(P, n, k, Dinv, status);
+      trsm_panel_kernel<<<tiles, 256, 0, stream>>>(P, n, k, status);
       note_launch();
       syrk_kernel<<<tiles * (tiles + 1) / 2, 256, 0, stream>>>(P, n, k, status);
       note_launch();
     }
   }
-  // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower)
-  for (int j = n - NB; j >= 0; j -= NB) {
-    trti2_kernel<<<1, 64, 0, stream>>>(P, n, j, Dinv, status);
-    note_launch();
+  // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower); the diagonal
+  // blocks were inverted by the factorisation
+  for (int j = n - 2 * NB; j >= 0; j -= NB) {
     const int rem = n - j - NB;
     const int tiles = (rem + 63) / 64;
-    if (rem > 0) {
-      trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
-      note_launch();
-    }
-    trinv_apply_kernel<<<tiles + 1, 256, 0, stream>>>(P, n, j, T, Dinv, status);
+    trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+    note_launch();
+    trinv_apply_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
     note_launch();
   }
   {

@@ -215,6 +215,139 @@ __global__ void __launch_bounds__(256) weighted_err_kernel(const uint8_t* __rest
   }
 }
 
+// ---------------------------------------------------------------------------- grouped launches
+// One CTA of 256 threads per superblock; CTAs find their tensor in the descriptor table.
+
+template <int T>
+__device__ __forceinline__ void grid_sb(const SbDesc& t, int64_t sb) {
+  constexpr int NS = (T == kQ4_K || T == kQ5_K) ? 8 : 16;
+  if (threadIdx.x < NS) {
+    float a, m;
+    grid_of<T>(t.raw + sb * block_bytes(T), threadIdx.x, a, m);
+    t.dl[sb * NS + threadIdx.x] = a;
+    if (t.ml) t.ml[sb * NS + threadIdx.x] = m;
+  }
+}
+
+template <int T>
+__device__ __forceinline__ void repack_sb(const SbDesc& t, int64_t sb) {
+  __shared__ int8_t c[256];
+  c[threadIdx.x] = t.codes[sb * 256 + threadIdx.x];
+  __syncthreads();
+  uint8_t* b = t.raw_w + sb * block_bytes(T);
+  const int th = threadIdx.x;
+  if (T == kQ2_K) {
+    if (th < 64) {
+      const int h = th >> 5, l = th & 31;
+      const int8_t* s = c + h * 128 + l;
+      b[16 + th] = (uint8_t)((s[0] & 3) | ((s[32] & 3) << 2) | ((s[64] & 3) << 4) | ((s[96] & 3) << 6));
+    }
+  } else if (T == kQ3_K) {
+    if (th < 32) {
+      uint8_t m = 0;
+      for (int j = 0; j < 8; j++) m |= (uint8_t)((c[32 * j + th] + 4 > 3 ? 1 : 0) << j);
+      b[th] = m;
+    } else if (th < 96) {
+      const int q = th - 32, h = q >> 5, l = q & 31;
+      uint8_t v = 0;
+      for (int k = 0; k < 4; k++) {
+        int x = c[h * 128 + 32 * k + l] + 4;
+        x = x > 3 ? x - 4 : x;
+        v |= (uint8_t)((x & 3) << (2 * k));
+      }
+      b[32 + q] = v;
+    }
+  } else if (T == kQ4_K || T == kQ5_K) {
+    const int off = (T == kQ5_K) ? 48 : 16;
+    if (th < 128) {
+      const int cc = th >> 5, l = th & 31;
+      int lo = c[cc * 64 + l], hi = c[cc * 64 + 32 + l];
+      if (T == kQ5_K) {
+        lo = lo > 15 ? lo - 16 : lo;
+        hi = hi > 15 ? hi - 16 : hi;
+      }
+      b[off + th] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+    } else if (T == kQ5_K && th < 160) {
+      const int l = th - 128;
+      uint8_t m = 0;
+      for (int cc = 0; cc < 4; cc++) {
+        m |= (uint8_t)((c[cc * 64 + l] > 15 ? 1 : 0) << (2 * cc));
+        m |= (uint8_t)((c[cc * 64 + 32 + l] > 15 ? 1 : 0) << (2 * cc + 1));
+      }
+      b[16 + l] = m;
+    }
+  } else {
+    if (th < 128) {
+      const int h = th >> 6, r = th & 63, l = r & 31;
+      const int base = h * 128 + l;
+      b[th] = (r < 32) ? (uint8_t)(((c[base] + 32) & 0xF) | (((c[base + 64] + 32) & 0xF) << 4))
+                       : (uint8_t)(((c[base + 32] + 32) & 0xF) | (((c[base + 96] + 32) & 0xF) << 4));
+    } else if (th < 192) {
+      const int q = th - 128, h = q >> 5, l = q & 31;
+      const int base = h * 128 + l;
+      b[128 + q] = (uint8_t)(((c[base] + 32) >> 4) | (((c[base + 32] + 32) >> 4) << 2) |
+                             (((c[base + 64] + 32) >> 4) << 4) | (((c[base + 96] + 32) >> 4) << 6));
+    }
+  }
+}
+
+template <int T>
+__device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t sb) {
+  constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
+  const uint8_t* b = t.raw + sb * block_bytes(T);
+  const int i = threadIdx.x;
+  float dl, ml;
+  grid_of<T>(b, i / SW, dl, ml);
+  float v = dl * (float)code_of<T>(b, i);
+  if (!(T == kQ3_K || T == kQ6_K)) v = v - ml;
+  const float d = v - t.x[sb * 256 + i];
+  const float wt = t.w ? t.w[(sb % t.nsb_row) * 256 + i] : 1.0f;
+  double acc = (double)(d * d * wt);
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ double red[8];
+  if ((i & 31) == 0) red[i >> 5] = acc;
+  __syncthreads();
+  if (i == 0) {
+    double s2 = 0.0;
+    for (int k = 0; k < 8; k++) s2 += red[k];
+    atomicAdd(t.err, s2);
+  }
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) sb_batch_kernel(const __grid_constant__ SbBatch b) {
+  int lo = 0, hi = b.count - 1;
+  const int64_t cta = blockIdx.x;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.d[mid].sb0 <= cta) lo = mid;
+    else hi = mid - 1;
+  }
+  const SbDesc& t = b.d[lo];
+  const int64_t sb = cta - t.sb0;
+#define CPK_SB_OP(T)                              \
+  if (OP == 0) grid_sb<T>(t, sb);                 \
+  else if (OP == 1) repack_sb<T>(t, sb);          \
+  else werr_sb<T>(t, sb);
+  switch (t.type) {
+    case kQ2_K: CPK_SB_OP(kQ2_K) break;
+    case kQ3_K: CPK_SB_OP(kQ3_K) break;
+    case kQ4_K: CPK_SB_OP(kQ4_K) break;
+    case kQ5_K: CPK_SB_OP(kQ5_K) break;
+    default: CPK_SB_OP(kQ6_K) break;
+  }
+#undef CPK_SB_OP
+}
+
+int launch_sb_batch(int op, const SbBatch& b, int64_t total_sb, cudaStream_t stream) {
+  if (b.count == 0 || total_sb == 0) return 0;
+  if (op == 0) sb_batch_kernel<0><<<(unsigned)total_sb, 256, 0, stream>>>(b);
+  else if (op == 1) sb_batch_kernel<1><<<(unsigned)total_sb, 256, 0, stream>>>(b);
+  else sb_batch_kernel<2><<<(unsigned)total_sb, 256, 0, stream>>>(b);
+  note_launch();
+  return 0;
+}
+
 #define CPK_DISPATCH_K(type, KERNEL_CALL) \
   switch (type) {                         \
     case kQ2_K: { constexpr int T = kQ2_K; KERNEL_CALL; } break; \

@@ -96,14 +96,15 @@ __device__ __forceinline__ float sb_sumsq_8(const float* sq, int sub) {
 // ---------------------------------------------------------------------------- Q2_K
 
 template <bool IMAT>
-__global__ void __launch_bounds__(256) q2k_encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
-                                                         int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out) {
+__device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
+                                                int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
+                                                int64_t blk) {
   constexpr int BB = 84;
   __shared__ __align__(16) float s_sq[IMAT ? 16 : 1][256];
   __shared__ __align__(16) uint8_t s_L[16][256];
   __shared__ __align__(16) uint8_t s_out[16 * BB];
   const int sbl = threadIdx.x >> 4, sub = threadIdx.x & 15;
-  const int64_t sb0 = (int64_t)blockIdx.x * 16;
+  const int64_t sb0 = blk * 16;
   const int64_t sb = sb0 + sbl;
   const bool valid = sb < nsb_total;
   float xv[16];
@@ -199,15 +200,16 @@ __global__ void __launch_bounds__(256) q2k_encode_kernel(const float* __restrict
 // ---------------------------------------------------------------------------- Q3_K
 
 template <bool IMAT>
-__global__ void __launch_bounds__(256) q3k_encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
-                                                         int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out) {
+__device__ __forceinline__ void q3k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
+                                                int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
+                                                int64_t blk) {
   constexpr int BB = 110;
   __shared__ __align__(16) float s_sq[IMAT ? 16 : 1][256];
   __shared__ __align__(16) uint8_t s_L[16][256];
   __shared__ __align__(16) uint8_t s_Ls[16][16];
   __shared__ __align__(16) uint8_t s_out[16 * BB];
   const int sbl = threadIdx.x >> 4, sub = threadIdx.x & 15;
-  const int64_t sb0 = (int64_t)blockIdx.x * 16;
+  const int64_t sb0 = blk * 16;
   const int64_t sb = sb0 + sbl;
   const bool valid = sb < nsb_total;
   float xv[16];
@@ -302,13 +304,14 @@ __global__ void __launch_bounds__(256) q3k_encode_kernel(const float* __restrict
 // ---------------------------------------------------------------------------- Q6_K
 
 template <bool IMAT>
-__global__ void __launch_bounds__(256) q6k_encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
-                                                         int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out) {
+__device__ __forceinline__ void q6k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
+                                                int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
+                                                int64_t blk) {
   constexpr int BB = 210;
   __shared__ __align__(16) uint8_t s_L[16][256];
   __shared__ __align__(16) uint8_t s_out[16 * BB + 16];
   const int sbl = threadIdx.x >> 4, sub = threadIdx.x & 15;
-  const int64_t sb0 = (int64_t)blockIdx.x * 16;
+  const int64_t sb0 = blk * 16;
   const int64_t sb = sb0 + sbl;
   const bool valid = sb < nsb_total;
   float xv[16], w[16], Lf[16];
@@ -377,15 +380,16 @@ __global__ void __launch_bounds__(256) q6k_encode_kernel(const float* __restrict
 // ---------------------------------------------------------------------------- Q4_K / Q5_K
 
 template <bool IMAT, bool Q5>
-__global__ void __launch_bounds__(256) q45k_encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
-                                                          int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out) {
+__device__ __forceinline__ void q45k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
+                                                 int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
+                                                 int64_t blk) {
   constexpr int BB = Q5 ? 176 : 144;
   constexpr int NMAX = Q5 ? 31 : 15;
   __shared__ __align__(16) float s_sq[IMAT ? 32 : 1][256];
   __shared__ __align__(16) uint8_t s_L[32][256];
   __shared__ __align__(16) uint8_t s_out[32 * BB];
   const int sbl = threadIdx.x >> 3, sub = threadIdx.x & 7;
-  const int64_t sb0 = (int64_t)blockIdx.x * 32;
+  const int64_t sb0 = blk * 32;
   const int64_t sb = sb0 + sbl;
   const bool valid = sb < nsb_total;
   float xv[32], w[32], Lf[32], scale, negmin;
@@ -600,7 +604,57 @@ __global__ void __launch_bounds__(128) q80_encode_kernel(const float* __restrict
   store_chunk(out + b0 * 34, s_out, (int)(nvalid * 34));
 }
 
+// ---------------------------------------------------------------------------- kernels
+
+// superblocks per 256-thread CTA for each type
+template <int TYPE> constexpr int sb_per_cta() { return (TYPE == kQ4_K || TYPE == kQ5_K) ? 32 : 16; }
+
+template <int TYPE, bool IMAT>
+__device__ __forceinline__ void encode_body(const float* x, const float* qw, int64_t nsb, int64_t nsb_row, uint8_t* out,
+                                            int64_t blk) {
+  if constexpr (TYPE == kQ2_K) q2k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
+  else if constexpr (TYPE == kQ3_K) q3k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
+  else if constexpr (TYPE == kQ4_K) q45k_encode_body<IMAT, false>(x, qw, nsb, nsb_row, out, blk);
+  else if constexpr (TYPE == kQ5_K) q45k_encode_body<IMAT, true>(x, qw, nsb, nsb_row, out, blk);
+  else q6k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
+}
+
+template <int TYPE, bool IMAT>
+__global__ void __launch_bounds__(256) encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
+                                                     int64_t nsb, int64_t nsb_row, uint8_t* __restrict__ out) {
+  encode_body<TYPE, IMAT>(x, qw, nsb, nsb_row, out, blockIdx.x);
+}
+
+// Grouped launch: every CTA finds its tensor in the descriptor table (sorted by first CTA).
+template <int TYPE, bool IMAT>
+__global__ void __launch_bounds__(256) encode_batch_kernel(const __grid_constant__ FitBatch b) {
+  int lo = 0, hi = b.count - 1;
+  const int64_t cta = blockIdx.x;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.d[mid].cta0 <= cta) lo = mid;
+    else hi = mid - 1;
+  }
+  const FitDesc& t = b.d[lo];
+  encode_body<TYPE, IMAT>(t.x, t.qw, t.nsb, t.nsb_row, t.out, cta - t.cta0);
+}
+
 // ---------------------------------------------------------------------------- launchers
+
+#define CPK_DISPATCH_ENC(type, imat, CALL)                                                  \
+  switch (type) {                                                                          \
+    case kQ2_K: if (imat) { constexpr int T = kQ2_K; constexpr bool I = true; CALL; }       \
+                else { constexpr int T = kQ2_K; constexpr bool I = false; CALL; } break;    \
+    case kQ3_K: if (imat) { constexpr int T = kQ3_K; constexpr bool I = true; CALL; }       \
+                else { constexpr int T = kQ3_K; constexpr bool I = false; CALL; } break;    \
+    case kQ4_K: if (imat) { constexpr int T = kQ4_K; constexpr bool I = true; CALL; }       \
+                else { constexpr int T = kQ4_K; constexpr bool I = false; CALL; } break;    \
+    case kQ5_K: if (imat) { constexpr int T = kQ5_K; constexpr bool I = true; CALL; }       \
+                else { constexpr int T = kQ5_K; constexpr bool I = false; CALL; } break;    \
+    case kQ6_K: if (imat) { constexpr int T = kQ6_K; constexpr bool I = true; CALL; }       \
+                else { constexpr int T = kQ6_K; constexpr bool I = false; CALL; } break;    \
+    default: return 1;                                                                     \
+  }
 
 int launch_quantize(int type, const float* x, int64_t nrow, int64_t n, const float* qw, uint8_t* out,
                     cudaStream_t stream) {
@@ -614,31 +668,22 @@ int launch_quantize(int type, const float* x, int64_t nrow, int64_t n, const flo
   const int64_t nsb_row = n / 256, total = nrow * nsb_row;
   if (total == 0) return 0;
   const bool im = qw != nullptr;
-  const unsigned g16 = (unsigned)((total + 15) / 16), g32 = (unsigned)((total + 31) / 32);
-  switch (type) {
-    case kQ2_K:
-      if (im) q2k_encode_kernel<true><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      else q2k_encode_kernel<false><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      break;
-    case kQ3_K:
-      if (im) q3k_encode_kernel<true><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      else q3k_encode_kernel<false><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      break;
-    case kQ4_K:
-      if (im) q45k_encode_kernel<true, false><<<g32, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      else q45k_encode_kernel<false, false><<<g32, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      break;
-    case kQ5_K:
-      if (im) q45k_encode_kernel<true, true><<<g32, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      else q45k_encode_kernel<false, true><<<g32, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      break;
-    case kQ6_K:
-      if (im) q6k_encode_kernel<true><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      else q6k_encode_kernel<false><<<g16, 256, 0, stream>>>(x, qw, total, nsb_row, out);
-      break;
-    default:
-      return 1;
-  }
+  CPK_DISPATCH_ENC(type, im, ({
+    const unsigned g = (unsigned)((total + sb_per_cta<T>() - 1) / sb_per_cta<T>());
+    encode_kernel<T, I><<<g, 256, 0, stream>>>(x, qw, total, nsb_row, out);
+  }));
+  note_launch();
+  return 0;
+}
+
+int64_t quantize_batch_ctas(int type, int64_t nsb) {
+  const int per = (type == kQ4_K || type == kQ5_K) ? 32 : 16;
+  return (nsb + per - 1) / per;
+}
+
+int launch_quantize_batch(int type, bool imat, const FitBatch& b, int64_t total_ctas, cudaStream_t stream) {
+  if (b.count == 0 || total_ctas == 0) return 0;
+  CPK_DISPATCH_ENC(type, imat, (encode_batch_kernel<T, I><<<(unsigned)total_ctas, 256, 0, stream>>>(b)));
   note_launch();
   return 0;
 }

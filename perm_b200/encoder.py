@@ -14,6 +14,7 @@ and always computes the stock baseline roundtrip(x, type, qw) for the statistics
     and the stats need no extra fit;
   * the weighted squared errors are reduced on the device; one device-to-host copy at the end.
 """
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -56,105 +57,218 @@ class Encoder:
         self.log = log
         self._ws = None
         self._fws = None
-        self._fstatus = None
+        self._fstreams = None
 
     # ---------------------------------------------------------------- factorisation
-    def factor(self, hessians, diags=None, _max_tries=6):
+    def factor(self, hessians, diags=None, _max_tries=6, n_streams=8):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
-        Returns {key: Factor}."""
+        Returns {key: Factor}.  Independent factorisations run concurrently on a pool of
+        streams (each a chain of small dependent kernels), joined back into the caller's
+        stream; all status words are read with one synchronisation."""
         torch = self.torch
         L = nat.lib()
-        keys = list(hessians)
-        pending = {}
-        for k in keys:
+        keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
+        if not keys:
+            return {}
+        main = self.stream if self.stream is not None else torch.cuda.current_stream()
+        nst = max(1, min(n_streams, len(keys)))
+        if getattr(self, "_fstreams", None) is None or len(self._fstreams) < nst:
+            self._fstreams = [torch.cuda.Stream() for _ in range(max(nst, n_streams))]
+            self._fws = [None] * len(self._fstreams)
+        ws_bytes = max(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])) for k in keys)
+        for i in range(nst):
+            if self._fws[i] is None or self._fws[i].numel() < ws_bytes:
+                self._fws[i] = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
+        ready = torch.cuda.Event()
+        ready.record(main)
+        out, pending = {}, {}
+        for i, k in enumerate(keys):
             H = hessians[k]
             n = int(H.shape[0])
             diag = diags[k] if diags is not None and k in diags else torch.diagonal(H).cpu().numpy()
             order = np.argsort(-diag) if self.act_order else np.arange(n)
             mean_diag = float(np.mean(np.asarray(diag, np.float64)[order]))
             base = mean_diag if mean_diag > 0.0 else 1.0
-            pending[k] = (order, base)
-        ws_bytes = max(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])) for k in keys) if keys else 0
-        if self._fws is None or self._fws.numel() < ws_bytes:
-            self._fws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
-        # one status word per key; the shared workspace serialises the factorisations on the stream
-        status = torch.zeros(max(1, len(keys)), dtype=torch.int32, device="cuda")
-        out, dev_orders = {}, {}
-        for i, k in enumerate(keys):
-            order, base = pending[k]
-            n = len(order)
-            od = torch.from_numpy(order.astype(np.int32)).to("cuda")
-            dev_orders[k] = od
+            pending[k] = order
+            od = torch.from_numpy(order.astype(np.int32)).to("cuda", non_blocking=False)
             U = torch.empty((n, n), dtype=torch.float32, device="cuda")
-            nat.check(L.cp_factor_u(nat.ptr(hessians[k]), n, nat.ptr(od), float(self.damp * base + 1e-8), nat.ptr(U),
-                                    nat.ptr(self._fws), ws_bytes, nat.ptr(status[i:i + 1]),
-                                    nat.stream_ptr(torch, self.stream)), f"factor[{k}]")
-            out[k] = Factor(U, order, od, self.damp)
-        st = status.cpu().numpy() if keys else np.zeros(0)
+            ut2 = torch.empty(L.cp_ef_u_bytes(n) // 4, dtype=torch.float32, device="cuda")
+            st = self._fstreams[i % nst]
+            st.wait_event(ready)
+            sp = nat.stream_ptr(torch, st)
+            ws = self._fws[i % nst]
+            nat.check(L.cp_factor_u(nat.ptr(H), n, nat.ptr(od), float(self.damp * base + 1e-8), nat.ptr(U),
+                                    nat.ptr(ws), ws.numel(), nat.ptr(status[i:i + 1]), sp), f"factor[{k}]")
+            nat.check(L.cp_ef_prepare_u(nat.ptr(U), n, nat.ptr(ut2), sp), "prepare_u")
+            out[k] = Factor(U, order, od, self.damp, ut2)
+        for i in range(nst):
+            ev = torch.cuda.Event()
+            ev.record(self._fstreams[i])
+            main.wait_event(ev)
+        st_host = status.cpu().numpy()
         for i, k in enumerate(keys):
-            if st[i] == 0:
+            if st_host[i] == 0:
                 continue
-            order, _ = pending[k]
+            order = pending[k]
             U, d = efm.factor_u_dev(hessians[k], order, damp=self.damp * 10.0, _max_tries=_max_tries - 1,
                                     diag_host=(diags or {}).get(k), stream=self.stream)
-            out[k] = Factor(U, order, dev_orders[k], d)
-        for k in keys:
-            out[k].ut2 = efm.prepare_u_dev(out[k].U, stream=self.stream)
+            out[k] = Factor(U, order, out[k].order_dev, d, efm.prepare_u_dev(U, stream=self.stream))
         return out
 
     # ---------------------------------------------------------------- tensors
-    def _workspace(self, nbytes):
-        if self._ws is None or self._ws.numel() < nbytes:
-            self._ws = self.torch.empty(nbytes, dtype=self.torch.uint8, device="cuda")
-        return self._ws
+    def _arena(self, jobs):
+        """Per-job scratch (codes, compensated weights, grid, sweep workspace, baseline bytes),
+        carved from a few flat buffers that are reused while the job shapes stay the same."""
+        torch = self.torch
+        L = nat.lib()
+        key = tuple((j.name, j.ttype, j.mode, int(j.x.shape[0]), int(j.x.shape[1])) for j in jobs)
+        if getattr(self, "_arena_key", None) == key:
+            return self._arena_views
+        sizes = {"codes": 0, "wcur": 0, "grid": 0, "work": 0, "base": 0}
+        plan = []
+        for j in jobs:
+            nrow, n = int(j.x.shape[0]), int(j.x.shape[1])
+            ent = {}
+            if j.mode == "EF":
+                sbw = nat.GRID[j.ttype][0]
+                ent["codes"] = (sizes["codes"], nrow * n)
+                sizes["codes"] += _al(nrow * n)
+                ent["wcur"] = (sizes["wcur"], nrow * n)
+                sizes["wcur"] += _al(nrow * n)
+                ent["dl"] = (sizes["grid"], nrow * (n // sbw))
+                sizes["grid"] += _al(nrow * (n // sbw))
+                ent["ml"] = (sizes["grid"], nrow * (n // sbw))
+                sizes["grid"] += _al(nrow * (n // sbw))
+                wb = L.cp_ef_sweep_workspace_bytes(nrow, n)
+                ent["work"] = (sizes["work"], wb // 4)
+                sizes["work"] += _al(wb // 4)
+            if j.mode == "wRTN(attn0-diag)":
+                rb = nrow * kq.row_bytes(j.ttype, n)
+                ent["base"] = (sizes["base"], rb)
+                sizes["base"] += _al(rb)
+            plan.append(ent)
+        self._arena_buf = {
+            "codes": torch.empty(max(1, sizes["codes"]), dtype=torch.int8, device="cuda"),
+            "wcur": torch.empty(max(1, sizes["wcur"]), dtype=torch.float32, device="cuda"),
+            "grid": torch.empty(max(1, sizes["grid"]), dtype=torch.float32, device="cuda"),
+            "work": torch.empty(max(1, sizes["work"]), dtype=torch.float32, device="cuda"),
+            "base": torch.empty(max(1, sizes["base"]), dtype=torch.uint8, device="cuda"),
+        }
+        views = []
+        for j, ent in zip(jobs, plan):
+            nrow, n = int(j.x.shape[0]), int(j.x.shape[1])
+            v = {}
+            for k, (off, cnt) in ent.items():
+                src = {"codes": "codes", "wcur": "wcur", "dl": "grid", "ml": "grid", "work": "work",
+                       "base": "base"}[k]
+                v[k] = self._arena_buf[src][off:off + cnt]
+            views.append(v)
+        self._arena_key, self._arena_views = key, views
+        return views
 
     def encode(self, jobs, factors, stats=True, outputs=None):
-        """Encode every job; returns ({name: raw uint8 on device}, {name: stats dict})."""
+        """Encode every job with grouped launches; returns ({name: raw uint8 on device},
+        {name: stats dict})."""
         torch = self.torch
         L = nat.lib()
         s = nat.stream_ptr(torch, self.stream)
-        ws_need = 0
+        views = self._arena(jobs)
+        raws = []
         for j in jobs:
-            if j.mode == "EF":
-                ws_need = max(ws_need, L.cp_ef_workspace_bytes(TYPE_ID[j.ttype], j.x.shape[0], j.x.shape[1]))
-        ws = self._workspace(ws_need) if ws_need else None
-        errs = torch.zeros((len(jobs), 2), dtype=torch.float64, device="cuda")
-        raws, bases = {}, {}
-        for idx, j in enumerate(jobs):
             nrow, n = int(j.x.shape[0]), int(j.x.shape[1])
             raw = outputs[j.name] if outputs is not None and j.name in outputs else \
                 torch.empty((nrow, kq.row_bytes(j.ttype, n)), dtype=torch.uint8, device="cuda")
-            base = None
+            raws.append(raw)
+        errs = torch.zeros((len(jobs), 2), dtype=torch.float64, device="cuda")
+        ef_idx = [i for i, j in enumerate(jobs) if j.mode == "EF"]
+
+        def fit_batch(items):  # items: (type, x, qw, out)
+            by_type = {}
+            for tt, x, qw, out in items:
+                by_type.setdefault(tt, []).append(nat.FitJob(nat.addr(x), nat.addr(qw), nat.addr(out),
+                                                             int(x.shape[0]), int(x.shape[1])))
+            for tt, lst in by_type.items():
+                arr = nat.job_array(nat.FitJob, lst)
+                nat.check(L.cp_kquant_encode_batch(TYPE_ID[tt], ctypes.cast(arr, ctypes.c_void_p), len(lst), s),
+                          "kquant_encode_batch")
+
+        def block_call(fn, items, what):
+            if not items:
+                return
+            arr = nat.job_array(nat.BlockJob, items)
+            nat.check(fn(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
+
+        def werr_items(idx_list, col, use_base=False):
+            out = []
+            for i in idx_list:
+                j = jobs[i]
+                src = views[i]["base"] if use_base else raws[i]
+                out.append(nat.BlockJob(TYPE_ID[j.ttype], nat.addr(src), None, None, nat.addr(j.x), nat.addr(j.qw),
+                                        None, None, errs[i, col].data_ptr(), int(j.x.shape[0]), int(j.x.shape[1])))
+            return out
+
+        # round 1 fits (EF from x) together with the weighted-RTN fits
+        items = []
+        for i, j in enumerate(jobs):
             if j.mode == "EF":
-                f = factors[j.hkey]
-                first = torch.empty_like(raw) if stats else None
-                nat.check(L.cp_ef_encode(TYPE_ID[j.ttype], nat.ptr(j.x), nrow, n, nat.ptr(f.order_dev), nat.ptr(f.ut2),
-                                         nat.ptr(j.qw), int(self.n_iter), nat.ptr(raw), nat.ptr(first), nat.ptr(ws),
-                                         ws.numel(), s), f"ef_encode[{j.name}]")
-                base = first
+                items.append((j.ttype, j.x, j.qw, raws[i]))
             elif j.mode == "wRTN(attn0-diag)":
-                kq.quantize_dev(j.ttype, j.x, j.fit_w, out=raw, stream=self.stream)
+                items.append((j.ttype, j.x, j.fit_w, raws[i]))
                 if stats:
-                    base = kq.quantize_dev(j.ttype, j.x, j.qw, stream=self.stream)
+                    items.append((j.ttype, j.x, j.qw, views[i]["base"].view(raws[i].shape)))
             elif j.mode == "wRTN":
-                kq.quantize_dev(j.ttype, j.x, j.qw, out=raw, stream=self.stream)
-                base = raw
+                items.append((j.ttype, j.x, j.qw, raws[i]))
             else:
                 raise ValueError(f"unknown mode {j.mode}")
-            if stats:
-                nat.check(L.cp_weighted_err(TYPE_ID[j.ttype], nat.ptr(raw), nat.ptr(j.x), nat.ptr(j.qw), nrow, n,
-                                            nat.ptr(errs[idx, 0:1]), s), "weighted_err")
-                if base is raw:
-                    errs[idx, 1:2].copy_(errs[idx, 0:1])
-                else:
-                    nat.check(L.cp_weighted_err(TYPE_ID[j.ttype], nat.ptr(base), nat.ptr(j.x), nat.ptr(j.qw), nrow, n,
-                                                nat.ptr(errs[idx, 1:2]), s), "weighted_err")
-            raws[j.name] = raw
+        fit_batch(items)
+        if stats:  # stock baseline = round-1 committed bytes (EF) or the separate qw fit (attn0)
+            block_call(L.cp_weighted_err_batch, werr_items(ef_idx, 1), "weighted_err_batch")
+            block_call(L.cp_weighted_err_batch,
+                       werr_items([i for i, j in enumerate(jobs) if j.mode == "wRTN(attn0-diag)"], 1, True),
+                       "weighted_err_batch")
+        for it in range(self.n_iter):
+            if it > 0:
+                fit_batch([(jobs[i].ttype, views[i]["wcur"].view(jobs[i].x.shape), jobs[i].qw, raws[i])
+                           for i in ef_idx])
+            grid = []
+            for i in ef_idx:
+                j = jobs[i]
+                hm = nat.GRID[j.ttype][3]
+                grid.append(nat.BlockJob(TYPE_ID[j.ttype], nat.addr(raws[i]), None, None, None, None,
+                                         nat.addr(views[i]["dl"]), nat.addr(views[i]["ml"]) if hm else None, None,
+                                         int(j.x.shape[0]), int(j.x.shape[1])))
+            block_call(L.cp_grid_params_batch, grid, "grid_params_batch")
+            sw = []
+            for i in ef_idx:
+                j = jobs[i]
+                f = factors[j.hkey]
+                hm = nat.GRID[j.ttype][3]
+                sw.append(nat.SweepJob(TYPE_ID[j.ttype], nat.addr(j.x), int(j.x.shape[0]), int(j.x.shape[1]),
+                                       nat.addr(f.order_dev), nat.addr(f.ut2), nat.addr(views[i]["dl"]),
+                                       nat.addr(views[i]["ml"]) if hm else None, nat.addr(views[i]["codes"]),
+                                       nat.addr(views[i]["wcur"]) if it + 1 < self.n_iter else None,
+                                       nat.addr(views[i]["work"])))
+            if sw:
+                arr = nat.job_array(nat.SweepJob, sw)
+                nat.check(L.cp_ef_sweep_batch(ctypes.cast(arr, ctypes.c_void_p), len(sw), s), "ef_sweep_batch")
+            rp = []
+            for i in ef_idx:
+                j = jobs[i]
+                rp.append(nat.BlockJob(TYPE_ID[j.ttype], None, nat.addr(raws[i]), nat.addr(views[i]["codes"]),
+                                       None, None, None, None, None, int(j.x.shape[0]), int(j.x.shape[1])))
+            block_call(L.cp_kquant_repack_batch, rp, "repack_batch")
         st = {}
         if stats:
+            block_call(L.cp_weighted_err_batch, werr_items(range(len(jobs)), 0), "weighted_err_batch")
             e = errs.cpu().numpy()
             for idx, j in enumerate(jobs):
-                e_ours, e_base = float(e[idx, 0]), float(e[idx, 1])
+                e_ours = float(e[idx, 0])
+                e_base = e_ours if j.mode == "wRTN" else float(e[idx, 1])
                 st[j.name] = {"type": j.ttype, "mode": j.mode,
                               "rel_err_vs_stock": e_ours / e_base - 1 if e_base else 0.0}
-        return raws, st
+        return {j.name: r for j, r in zip(jobs, raws)}, st
+
+
+def _al(n, a=64):
+    return (n + a - 1) // a * a

@@ -1,0 +1,68 @@
+"""Grouped (multi-tensor) launches vs the oracle: the whole-model encoder must produce the
+same bytes as the per-tensor reference semantics."""
+import numpy as np
+import pytest
+
+from conftest import K_TYPES
+
+pytestmark = pytest.mark.gpu
+
+
+def _hessian(rng, n, T=2048):
+    X = rng.standard_normal((T, n)) * rng.lognormal(0, 1, n)
+    return X.T @ X / T
+
+
+def _encode(jobs_np, hess_np, stats=True):
+    import torch
+    from perm_b200.encoder import Encoder, Job
+    hd = {k: torch.from_numpy(H).cuda() for k, H in hess_np.items()}
+    diags = {k: np.diag(H) for k, H in hess_np.items()}
+    jobs = []
+    for name, tt, mode, W, qw, hk, fw in jobs_np:
+        jobs.append(Job(name, tt, mode, torch.from_numpy(W).cuda(),
+                        None if qw is None else torch.from_numpy(qw).cuda(), hk,
+                        None if fw is None else torch.from_numpy(fw).cuda()))
+    enc = Encoder()
+    factors = enc.factor(hd, diags)
+    raws, st = enc.encode(jobs, factors, stats=stats)
+    return {k: v.cpu().numpy() for k, v in raws.items()}, st
+
+
+@pytest.mark.parametrize("many_rows", [False, True])
+def test_grouped_encode_matches_oracle(orc, many_rows):
+    rng = np.random.default_rng(3)
+    n = 256
+    hess = {"a": _hessian(rng, n), "b": _hessian(rng, 512)}
+    rows = 1024 if many_rows else 40      # 20 x 1024 rows selects the one-warp sweep variant
+    jobs = []
+    for i in range(20 if many_rows else 6):
+        tt = K_TYPES[i % 5]
+        hk = "a" if i % 2 == 0 else "b"
+        nn = hess[hk].shape[0]
+        W = (rng.standard_normal((rows if i else rows + 3, nn)) * 0.02).astype(np.float32)
+        jobs.append((f"t{i}", tt, "EF", W, np.diag(hess[hk]).astype(np.float32), hk, None))
+    Wemb = (rng.standard_normal((77, n)) * 0.02).astype(np.float32)
+    jobs.append(("embd", "Q2_K", "wRTN(attn0-diag)", Wemb, None, "a", np.diag(hess["a"]).astype(np.float32)))
+    got, st = _encode(jobs, hess)
+    for name, tt, mode, W, qw, hk, fw in jobs:
+        if mode == "EF":
+            want, _ = orc.ef_encode(W, tt, qw, hess[hk], n_iter=2, act_order=True)
+        else:
+            want = orc.quantize(tt, W, fw)
+        assert np.array_equal(got[name], want), f"{name} {tt}: {np.count_nonzero(got[name] != want)} bytes differ"
+    assert set(st) == {j[0] for j in jobs}
+    assert all(np.isfinite(v["rel_err_vs_stock"]) for v in st.values())
+
+
+def test_grouped_stats_match_reference_formula(orc):
+    rng = np.random.default_rng(9)
+    H = _hessian(rng, 512)
+    W = (rng.standard_normal((64, 512)) * 0.02).astype(np.float32)
+    qw = np.diag(H).astype(np.float32)
+    got, st = _encode([("w", "Q3_K", "EF", W, qw, "h", None)], {"h": H})
+    recon = orc.dequantize("Q3_K", got["w"], 512)
+    base = orc.roundtrip(W, "Q3_K", qw)
+    e_ours = float(((((recon - W) ** 2) * qw).astype(np.float64)).sum())
+    e_base = float(((((base - W) ** 2) * qw).astype(np.float64)).sum())
+    assert abs(st["w"]["rel_err_vs_stock"] - (e_ours / e_base - 1)) < 1e-6
