@@ -170,6 +170,19 @@ typedef struct {
 /* ef.py:197-216 for every job in one launch (a CTA per 32 rows of any job). */
 int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream);
 
+typedef struct {
+  const double* H;       /* [n, n] */
+  int64_t n;             /* multiple of 64 */
+  const int32_t* order;  /* act-order permutation [n] */
+  double diag_shift;     /* damp * mean(diag(H[order][:,order])) + 1e-8 */
+  float* U_out;          /* [n, n] float32 upper factor */
+  void* workspace;       /* cp_factor_workspace_bytes(n) bytes, one per job */
+  int32_t* status_dev;   /* device int32: 0, or CP_ERR_NOT_PD */
+} cp_factor_job;
+/* ef.py:46-84 for every job: jobs of the same n advance through each factorisation step in
+ * one launch (up to 64 per launch). */
+int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream);
+
 /* hessians.py:455-470 hook arithmetic: H += x^T x for x bf16 [T, d] (row-major, d a
  * multiple of 128), H float32 [d, d], accumulated in float32 on the tensor cores. */
 int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream);

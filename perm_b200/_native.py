@@ -48,6 +48,12 @@ def job_array(cls, items):
     return arr
 
 
+class FactorJob(ctypes.Structure):
+    _fields_ = [("H", ctypes.c_void_p), ("n", ctypes.c_int64), ("order", ctypes.c_void_p),
+                ("diag_shift", ctypes.c_double), ("U_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+                ("status_dev", ctypes.c_void_p)]
+
+
 class CudaPathError(RuntimeError):
     """A CUDA call of the encoder failed (launch error, bad argument, missing library)."""
 
@@ -93,6 +99,7 @@ def lib():
         "cp_kquant_repack_batch": ([P, I, P], I),
         "cp_weighted_err_batch": ([P, I, P], I),
         "cp_ef_sweep_batch": ([P, I, P], I),
+        "cp_factor_u_batch": ([P, I, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

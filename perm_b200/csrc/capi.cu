@@ -415,6 +415,40 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   return CP_OK;
 }
 
+int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream) {
+  if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
+  cudaStream_t s = (cudaStream_t)stream;
+  std::vector<int> done(count, 0);
+  static thread_local cpk::FactorBatch fb;
+  for (int i = 0; i < count; i++) {
+    const cp_factor_job& j = jobs[i];
+    if (j.n <= 0 || j.n % 64 || j.n > 65536) return set_err(CP_ERR_SHAPE, "n must be a positive multiple of 64");
+    if (!j.H || !j.order || !j.U_out || !j.workspace || !j.status_dev) return set_err(CP_ERR_ARG, "null pointer");
+    if (((uintptr_t)j.workspace) & 15) return set_err(CP_ERR_ARG, "workspace must be 16-byte aligned");
+  }
+  for (int i = 0; i < count; i++) {
+    if (done[i]) continue;
+    fb.count = 0;
+    fb.n = (int)jobs[i].n;
+    fb.out_f64 = 0;
+    for (int k = i; k < count && fb.count < cpk::kFactorBatchMax; k++) {
+      if (done[k] || jobs[k].n != jobs[i].n) continue;
+      const int b = fb.count++;
+      fb.H[b] = jobs[k].H;
+      fb.order[b] = jobs[k].order;
+      fb.P[b] = (double*)jobs[k].workspace;
+      fb.U[b] = jobs[k].U_out;
+      fb.status[b] = jobs[k].status_dev;
+      fb.shift[b] = jobs[k].diag_shift;
+      done[k] = 1;
+    }
+    ProfScope ps(kProfFactor, s);
+    if (int rc = check_rc(cpk::launch_factor_batch(fb, s), "cp_factor_u_batch")) return rc;
+    i--;  // revisit: there may be more jobs of this size than one batch holds
+  }
+  return CP_OK;
+}
+
 int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream) {
   if (T < 0 || d <= 0 || d % 128) return set_err(CP_ERR_SHAPE, "d must be a positive multiple of 128");
   if (T == 0) return CP_OK;

@@ -32,6 +32,18 @@ int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int
                     const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
                     int8_t* codes, float* wcur, cudaStream_t stream);
 size_t factor_workspace_bytes(int64_t n);
+// Same-size factorisations advanced step by step together (grid y / z index the item).
+constexpr int kFactorBatchMax = 64;
+struct FactorBatch {
+  int count, n, out_f64;
+  const double* H[kFactorBatchMax];
+  const int* order[kFactorBatchMax];
+  double* P[kFactorBatchMax];     // workspace of factor_workspace_bytes(n) each
+  void* U[kFactorBatchMax];
+  int* status[kFactorBatchMax];
+  double shift[kFactorBatchMax];
+};
+int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream);
 int launch_factor_u(const double* H, int64_t n, const int* order, double shift, void* U, bool out_f64,
                     void* work, int* status, cudaStream_t stream);
 }  // namespace cpk

@@ -1,7 +1,7 @@
 // FP64 factorization for error feedback: U = chol(inv(Hd)).T, the upper-triangular factor of
 // coldpress/ef.py:46-84 (cholesky_inv_upper) cast to float32, computed on the GPU as
 //     P  = J * Hd[order][:, order] * J          (act-order permutation, then reversal J)
-//     P  = L L^T                                (blocked right-looking Cholesky, nb = 64)
+//     P  = L L^T                                (blocked left-looking Cholesky, nb = 64)
 //     U  = J * L^{-1} * J                       (blocked triangular inverse, then reversal)
 // Because Hd = (J L J)(J L J)^T with J L J upper, (J L^{-1} J) is the unique upper factor
 // with U^T U = inv(Hd): the same matrix as the reference's inv-then-cholesky route, in one
@@ -18,221 +18,246 @@ namespace cpk {
 constexpr int NB = 64;
 
 // P[i][j] = H[order[n-1-i]][order[n-1-j]] (+ shift on the diagonal).  Only the lower
-// triangle is consumed; the strict upper triangle is written as zero.
-__global__ void permute_reverse_kernel(const double* __restrict__ H, int n, const int* __restrict__ order,
-                                       double shift, double* __restrict__ P) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+// triangle is consumed; the strict upper triangle is written as zero.  blockIdx.z: item.
+__global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
+  const int n = fb.n;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y, b = blockIdx.z;
   if (j >= n) return;
+  const int* order = fb.order[b];
   double v = 0.0;
   if (j <= i) {
-    v = H[(size_t)order[n - 1 - i] * n + order[n - 1 - j]];
-    if (i == j) v += shift;
+    v = fb.H[b][(size_t)order[n - 1 - i] * n + order[n - 1 - j]];
+    if (i == j) v += fb.shift[b];
   }
-  P[(size_t)i * n + j] = v;
+  fb.P[b][(size_t)i * n + j] = v;
 }
 
 // Diagonal block at (k, k): Cholesky factor L11 of the (already updated) block, then its
-// inverse, written in place of the block.  One warp; lane l owns rows l and l + 32 and the
-// block lives in shared memory.  Nothing after this step needs L11 itself: the panel below is
-// solved with inv(L11) and the diagonal blocks of L^-1 are exactly these inverses.
+// inverse, written in place of the block.  Nothing after this step needs L11 itself: the
+// panel below is solved with inv(L11) and the diagonal blocks of L^-1 are exactly these
+// inverses.  256 threads, block in shared memory: each Cholesky column step scales the
+// column and updates the trailing triangle element-parallel; each inverse column step forms
+// the row dot products with four threads per row and a shuffle reduction.
 // A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
-__global__ void __launch_bounds__(32) potrf_inv_diag_kernel(double* __restrict__ A, int n, int k,
-                                                            int* __restrict__ status) {
+__global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k) {
   __shared__ double a[NB][NB + 1];
-  const int l = threadIdx.x;
+  __shared__ double piv[NB];
+  const int t = threadIdx.x;
+  const int n = fb.n;
+  double* __restrict__ A = fb.P[blockIdx.x];
+  int* status = fb.status[blockIdx.x];
   if (*status) return;
-  for (int i = l; i < NB * NB; i += 32) {
+  for (int i = t; i < NB * NB; i += 256) {
     const int r = i / NB, c = i % NB;
     a[r][c] = (c <= r) ? A[(size_t)(k + r) * n + k + c] : 0.0;
   }
-  __syncwarp();
-  const int rows[2] = {l, l + 32};
+  __syncthreads();
   for (int j = 0; j < NB; j++) {
     const double d = a[j][j];
-    if (!(d > 0.0)) {  // uniform: every lane read the same pivot
-      if (l == 0) *status = 1;
+    if (!(d > 0.0)) {  // uniform: every thread read the same pivot
+      if (t == 0) *status = 1;
       return;
     }
-    const double s = sqrt(d);
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int r = rows[q];
-      if (r == j) a[r][j] = s;
-      else if (r > j) a[r][j] /= s;
+    const double sq = sqrt(d);
+    if (t == 0) piv[j] = sq;
+    const int m = NB - 1 - j;
+    if (t < m) a[j + 1 + t][j] /= sq;
+    __syncthreads();
+    for (int idx = t; idx < m * m; idx += 256) {
+      const int r = j + 1 + idx / m, c = j + 1 + idx % m;
+      if (c <= r) a[r][c] = fma(-a[r][j], a[c][j], a[r][c]);
     }
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int r = rows[q];
-      if (r > j) {
-        const double v = a[r][j];
-        for (int c = j + 1; c <= r; c++) a[r][c] = fma(-v, a[c][j], a[r][c]);
-      }
-    }
-    __syncwarp();
+    __syncthreads();
   }
+  if (t < NB) a[t][t] = piv[t];
+  __syncthreads();
   // in-place inverse of the lower-triangular block, columns right to left (LAPACK dtrti2)
+  const int g = t >> 2, q = t & 3;  // row group g (0..63), lane q within it
   for (int j = NB - 1; j >= 0; j--) {
     const double inv_jj = 1.0 / a[j][j];
-    double acc[2] = {0.0, 0.0};
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int i = rows[q];
-      if (i > j) {
-        double t = 0.0;
-        for (int kk = j + 1; kk <= i; kk++) t = fma(a[i][kk], a[kk][j], t);
-        acc[q] = t;
-      }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int i = rows[q];
-      if (i > j) a[i][j] = -inv_jj * acc[q];
+    const int i = g;
+    double acc = 0.0;
+    if (i > j)
+      for (int kk = j + 1 + q; kk <= i; kk += 4) acc = fma(a[i][kk], a[kk][j], acc);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    __syncthreads();
+    if (q == 0) {
+      if (i > j) a[i][j] = -inv_jj * acc;
       else if (i == j) a[i][j] = inv_jj;
     }
-    __syncwarp();
+    __syncthreads();
   }
-  for (int i = l; i < NB * NB; i += 32) {
+  for (int i = t; i < NB * NB; i += 256) {
     const int r = i / NB, c = i % NB;
     A[(size_t)(k + r) * n + k + c] = (c <= r) ? a[r][c] : 0.0;
   }
 }
 
-// Tile GEMM: C[64x64 tile] = alpha * sum_l A[i][l] * Bop[l][j] (+ beta * C), FP64 on CUDA
-// cores, 256 threads with a 4x4 register tile each, K streamed in chunks of 16 through
-// shared memory.  B_TRANS: Bop[l][j] = B[j][l] (A*B^T), else Bop[l][j] = B[l][j].
-template <bool B_TRANS>
-__device__ __forceinline__ void tile_gemm(const double* __restrict__ A, int lda, const double* __restrict__ B,
-                                          int ldb, int m_lim, int n_lim, int k_len, double (&acc)[4][4]) {
-  __shared__ double sa[16][64 + 1];
-  __shared__ double sb[16][64 + 1];
-  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool ok) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  const int src_bytes = ok ? 16 : 0;  // 0: nothing is read, the 16 bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
+}
+
+// 64 x 64 FP64 tile product on CUDA cores: acc = sum_l A[i][l] * Bop[l][j] over l < k_len.
+// 64 threads, each an 8 x 8 register tile (rows tm + 8r, columns tn + 8c); K streamed in chunks
+// of 16 through a two-stage cp.async pipeline (rows padded to 18 doubles: conflict-free).
+// B_NK: B is stored [N][K] (Bop = B^T, the A*B^T form); otherwise B is [K][N].
+// Rows >= m_lim of A and columns >= n_lim of Bop read as zero.
+template <bool B_NK>
+__device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, const double* __restrict__ B, int ldb,
+                                       int m_lim, int n_lim, int k_len, double (&acc)[8][8]) {
+  __shared__ __align__(16) double sa[2][64][18];
+  __shared__ __align__(16) double sb[2][64][18];   // [N][K] chunk (B_NK) or [K][N] packed as [16][66] below
+  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int i = 0; i < 8; i++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
-  for (int l0 = 0; l0 < k_len; l0 += 16) {
-    for (int i = t; i < 16 * 64; i += 256) {
-      const int r = i / 16, l = i % 16;  // A row r, column l0+l
-      sa[l][r] = (r < m_lim && l0 + l < k_len) ? A[(size_t)r * lda + l0 + l] : 0.0;
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+  auto load = [&](int l0, int buf) {
+#pragma unroll
+    for (int q = 0; q < 8; q++) {  // A chunk: 64 rows x 16 doubles = 512 x 16 bytes
+      const int i = t + 64 * q, r = i >> 3, kk = (i & 7) * 2;
+      const bool ok = r < m_lim && l0 + kk < k_len;
+      cp_async16_zfill(&sa[buf][r][kk], ok ? (const void*)(A + (size_t)r * lda + l0 + kk) : (const void*)A, ok);
     }
-    if (B_TRANS) {
-      for (int i = t; i < 16 * 64; i += 256) {
-        const int c = i / 16, l = i % 16;
-        sb[l][c] = (c < n_lim && l0 + l < k_len) ? B[(size_t)c * ldb + l0 + l] : 0.0;
+    if (B_NK) {
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const int i = t + 64 * q, c = i >> 3, kk = (i & 7) * 2;
+        const bool ok = c < n_lim && l0 + kk < k_len;
+        cp_async16_zfill(&sb[buf][c][kk], ok ? (const void*)(B + (size_t)c * ldb + l0 + kk) : (const void*)B, ok);
       }
     } else {
-      for (int i = t; i < 16 * 64; i += 256) {
-        const int l = i / 64, c = i % 64;
-        sb[l][c] = (c < n_lim && l0 + l < k_len) ? B[(size_t)(l0 + l) * ldb + c] : 0.0;
+      double* sbk = &sb[buf][0][0];  // viewed as [16][72]: row kk holds Bop[kk][0..63]
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const int i = t + 64 * q, kk = i >> 5, c = (i & 31) * 2;
+        const bool ok = c < n_lim && l0 + kk < k_len;
+        cp_async16_zfill(sbk + kk * 72 + c, ok ? (const void*)(B + (size_t)(l0 + kk) * ldb + c) : (const void*)B, ok);
       }
     }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  if (k_len <= 0) return;
+  load(0, 0);
+  int buf = 0;
+  for (int l0 = 0; l0 < k_len; l0 += 16, buf ^= 1) {
+    if (l0 + 16 < k_len) {
+      load(l0 + 16, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    }
     __syncthreads();
+    const double* sbk = &sb[buf][0][0];
 #pragma unroll
-    for (int l = 0; l < 16; l++) {
-      double av[4], bv[4];
+    for (int kk = 0; kk < 16; kk++) {
+      double av[8], bv[8];
 #pragma unroll
-      for (int i = 0; i < 4; i++) av[i] = sa[l][tr + 16 * i];
+      for (int r = 0; r < 8; r++) av[r] = sa[buf][tm + 8 * r][kk];
 #pragma unroll
-      for (int j = 0; j < 4; j++) bv[j] = sb[l][tc + 16 * j];
+      for (int c = 0; c < 8; c++) bv[c] = B_NK ? sb[buf][tn + 8 * c][kk] : sbk[kk * 72 + tn + 8 * c];
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int r = 0; r < 8; r++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+        for (int c = 0; c < 8; c++) acc[r][c] = fma(av[r], bv[c], acc[r][c]);
     }
     __syncthreads();
   }
 }
 
-// Panel below the diagonal block: A21 := A21 * inv(L11)^T, inv(L11) read from the diagonal.
-__global__ void __launch_bounds__(256) trsm_panel_kernel(double* __restrict__ A, int n, int k, const int* status) {
-  if (*status) return;
-  const int r0 = k + NB + blockIdx.x * 64;
-  const int m = min(64, n - r0);
-  const int nb = min(NB, n - k);
-  double acc[4][4];
-  // out[r][c] = sum_l A21[r][l] * inv(L11)[c][l]
-  tile_gemm<true>(A + (size_t)r0 * n + k, n, A + (size_t)k * n + k, n, m, nb, nb, acc);
-  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+// Left-looking Cholesky step j, before the diagonal factorisation:
+//   A[j:n, j:j+64] -= L[j:n, 0:j] * L[j:j+64, 0:j]^T        (one 64-row tile per CTA)
+__global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j) {
+  const int n = fb.n;
+  double* __restrict__ A = fb.P[blockIdx.y];
+  if (*fb.status[blockIdx.y]) return;
+  const int r0 = j + blockIdx.x * 64;
+  double acc[8][8];
+  tile64<true>(A + (size_t)r0 * n, n, A + (size_t)j * n, n, n - r0, 64, j, acc);
+  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int r = 0; r < 8; r++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int r = tr + 16 * i, c = tc + 16 * j;
-      if (r < m && c < nb) A[(size_t)(r0 + r) * n + k + c] = acc[i][j];
+    for (int c = 0; c < 8; c++) {
+      const int rr = r0 + tm + 8 * r, cc = j + tn + 8 * c;
+      if (rr < n && rr >= cc) A[(size_t)rr * n + cc] -= acc[r][c];
     }
 }
 
-// Trailing update A22 -= A21 A21^T on lower 64x64 tiles.
-__global__ void __launch_bounds__(256) syrk_kernel(double* __restrict__ A, int n, int k, const int* status) {
-  if (*status) return;
-  // blockIdx.x enumerates lower tiles (ti >= tj) of the trailing matrix
-  int idx = blockIdx.x, ti = 0;
-  while (idx > ti) { idx -= ti + 1; ti++; }
-  const int tj = idx;
-  const int base = k + NB;
-  const int r0 = base + ti * 64, c0 = base + tj * 64;
-  const int m = min(64, n - r0), nn = min(64, n - c0);
-  double acc[4][4];
-  tile_gemm<true>(A + (size_t)r0 * n + k, n, A + (size_t)c0 * n + k, n, m, nn, NB, acc);
-  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+// Panel below the diagonal block: A[j+64:n, j:j+64] := A * inv(L_jj)^T (inverse on the diagonal).
+__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
+  const int n = fb.n;
+  double* __restrict__ A = fb.P[blockIdx.y];
+  if (*fb.status[blockIdx.y]) return;
+  const int r0 = j + 64 + blockIdx.x * 64;
+  double acc[8][8];
+  tile64<true>(A + (size_t)r0 * n + j, n, A + (size_t)j * n + j, n, n - r0, 64, 64, acc);
+  __syncthreads();  // every CTA reads only its own rows of the panel, so in-place is safe
+  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int r = 0; r < 8; r++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int r = tr + 16 * i, c = tc + 16 * j;
-      if (r < m && c < nn && r0 + r >= c0 + c) A[(size_t)(r0 + r) * n + c0 + c] -= acc[i][j];
+    for (int c = 0; c < 8; c++) {
+      const int rr = r0 + tm + 8 * r;
+      if (rr < n) A[(size_t)rr * n + j + tn + 8 * c] = acc[r][c];
     }
 }
 
 // Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
-//   T   = -Linv22 * L21          (rows below, into scratch)
-__global__ void __launch_bounds__(256) trmm_kernel(const double* __restrict__ A, int n, int j,
-                                                   double* __restrict__ T, const int* status) {
-  if (*status) return;
+//   T = -Linv22 * L21          (rows below, into scratch; Linv22 is lower triangular)
+__global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ FactorBatch fb, int j) {
+  const int n = fb.n;
+  const double* __restrict__ A = fb.P[blockIdx.y];
+  double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
+  if (*fb.status[blockIdx.y]) return;
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
-  // rows r0.. of Linv22 have nonzeros only in columns base .. r0+m-1
-  const int k_len = r0 + m - base;
-  double acc[4][4];
-  tile_gemm<false>(A + (size_t)r0 * n + base, n, A + (size_t)base * n + j, n, m, NB, k_len, acc);
-  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+  const int k_len = r0 + m - base;  // rows r0.. of Linv22 vanish right of column r0+m-1
+  double acc[8][8];
+  tile64<false>(A + (size_t)r0 * n + base, n, A + (size_t)base * n + j, n, m, 64, k_len, acc);
+  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int r = 0; r < 8; r++)
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const int r = tr + 16 * i, cc = tc + 16 * c;
-      if (r < m) T[(size_t)(r0 - base + r) * NB + cc] = -acc[i][c];
+    for (int c = 0; c < 8; c++) {
+      const int rr = tm + 8 * r;
+      if (rr < m) T[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = -acc[r][c];
     }
 }
 
-//   L21 := T * inv(L11)   (inv(L11) already sits on the diagonal)
-__global__ void __launch_bounds__(256) trinv_apply_kernel(double* __restrict__ A, int n, int j,
-                                                          const double* __restrict__ T, const int* status) {
-  if (*status) return;
+//   L21 := T * inv(L_jj)   (inv(L_jj) already sits on the diagonal)
+__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
+  const int n = fb.n;
+  double* __restrict__ A = fb.P[blockIdx.y];
+  const double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
+  if (*fb.status[blockIdx.y]) return;
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
-  double acc[4][4];
-  tile_gemm<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, NB, NB, acc);
-  const int t = threadIdx.x, tr = t / 16, tc = t % 16;
+  double acc[8][8];
+  tile64<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, 64, 64, acc);
+  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int r = 0; r < 8; r++)
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const int r = tr + 16 * i, cc = tc + 16 * c;
-      if (r < m) A[(size_t)(r0 + r) * n + j + cc] = acc[i][c];
+    for (int c = 0; c < 8; c++) {
+      const int rr = tm + 8 * r;
+      if (rr < m) A[(size_t)(r0 + rr) * n + j + tn + 8 * c] = acc[r][c];
     }
 }
 
 // U[i][j] = Linv[n-1-i][n-1-j] for j >= i, else 0 (cast to OutT).
 template <typename OutT>
-__global__ void unreverse_cast_kernel(const double* __restrict__ Linv, int n, OutT* __restrict__ U) {
+__global__ void unreverse_cast_kernel(const __grid_constant__ FactorBatch fb) {
+  const int n = fb.n;
   const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
   if (j >= n) return;
+  const double* __restrict__ Linv = fb.P[blockIdx.z];
+  OutT* __restrict__ U = (OutT*)fb.U[blockIdx.z];
   U[(size_t)i * n + j] = (j >= i) ? (OutT)Linv[(size_t)(n - 1 - i) * n + (n - 1 - j)] : (OutT)0;
 }
 
@@ -241,47 +266,60 @@ size_t factor_workspace_bytes(int64_t n) {
   return ((size_t)n * n + (size_t)n * NB) * sizeof(double);
 }
 
-int launch_factor_u(const double* H, int64_t n64, const int* order, double shift, void* U, bool out_f64,
-                    void* work, int* status, cudaStream_t stream) {
-  if (n64 <= 0 || n64 % NB) return 2;
-  const int n = (int)n64;
-  double* P = (double*)work;
-  double* T = P + (size_t)n * n;
-  cudaMemsetAsync(status, 0, sizeof(int), stream);
+int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
+  const int n = fb.n, cnt = fb.count;
+  if (cnt <= 0) return 0;
+  if (n <= 0 || n % NB) return 2;
+  for (int b = 0; b < cnt; b++) cudaMemsetAsync(fb.status[b], 0, sizeof(int), stream);
   {
-    dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
-    permute_reverse_kernel<<<g, 256, 0, stream>>>(H, n, order, shift, P);
+    dim3 g((unsigned)((n + 255) / 256), (unsigned)n, (unsigned)cnt);
+    permute_reverse_kernel<<<g, 256, 0, stream>>>(fb);
     note_launch();
   }
-  for (int k = 0; k < n; k += NB) {
-    potrf_inv_diag_kernel<<<1, 32, 0, stream>>>(P, n, k, status);
-    note_launch();
-    const int rem = n - k - NB;
-    if (rem > 0) {
-      const int tiles = (rem + 63) / 64;
-      trsm_panel_kernel<<<tiles, 256, 0, stream>>>(P, n, k, status);
+  for (int j = 0; j < n; j += NB) {
+    if (j > 0) {
+      chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
       note_launch();
-      syrk_kernel<<<tiles * (tiles + 1) / 2, 256, 0, stream>>>(P, n, k, status);
+    }
+    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j);
+    note_launch();
+    if (n - j - NB > 0) {
+      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
       note_launch();
     }
   }
   // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower); the diagonal
   // blocks were inverted by the factorisation
   for (int j = n - 2 * NB; j >= 0; j -= NB) {
-    const int rem = n - j - NB;
-    const int tiles = (rem + 63) / 64;
-    trmm_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+    const unsigned tiles = (unsigned)((n - j - NB + 63) / 64);
+    trmm_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
     note_launch();
-    trinv_apply_kernel<<<tiles, 256, 0, stream>>>(P, n, j, T, status);
+    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
     note_launch();
   }
   {
-    dim3 g((unsigned)((n + 255) / 256), (unsigned)n);
-    if (out_f64) unreverse_cast_kernel<double><<<g, 256, 0, stream>>>(P, n, (double*)U);
-    else unreverse_cast_kernel<float><<<g, 256, 0, stream>>>(P, n, (float*)U);
+    dim3 g((unsigned)((n + 255) / 256), (unsigned)n, (unsigned)cnt);
+    if (fb.out_f64) unreverse_cast_kernel<double><<<g, 256, 0, stream>>>(fb);
+    else unreverse_cast_kernel<float><<<g, 256, 0, stream>>>(fb);
     note_launch();
   }
   return 0;
+}
+
+int launch_factor_u(const double* H, int64_t n64, const int* order, double shift, void* U, bool out_f64,
+                    void* work, int* status, cudaStream_t stream) {
+  if (n64 <= 0 || n64 % NB) return 2;
+  FactorBatch fb;
+  fb.count = 1;
+  fb.n = (int)n64;
+  fb.out_f64 = out_f64 ? 1 : 0;
+  fb.H[0] = H;
+  fb.order[0] = order;
+  fb.P[0] = (double*)work;
+  fb.U[0] = U;
+  fb.status[0] = status;
+  fb.shift[0] = shift;
+  return launch_factor_batch(fb, stream);
 }
 
 }  // namespace cpk

@@ -60,29 +60,24 @@ class Encoder:
         self._fstreams = None
 
     # ---------------------------------------------------------------- factorisation
-    def factor(self, hessians, diags=None, _max_tries=6, n_streams=8):
+    def factor(self, hessians, diags=None, _max_tries=6):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
-        Returns {key: Factor}.  Independent factorisations run concurrently on a pool of
-        streams (each a chain of small dependent kernels), joined back into the caller's
-        stream; all status words are read with one synchronisation."""
+        Returns {key: Factor}.  All first attempts go out as one batched call (same-size
+        Hessians advance through each factorisation step in a single launch); the status
+        words are read with one synchronisation and only a non-positive pivot triggers the
+        reference's damp escalation for that Hessian."""
         torch = self.torch
         L = nat.lib()
         keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
         if not keys:
             return {}
-        main = self.stream if self.stream is not None else torch.cuda.current_stream()
-        nst = max(1, min(n_streams, len(keys)))
-        if getattr(self, "_fstreams", None) is None or len(self._fstreams) < nst:
-            self._fstreams = [torch.cuda.Stream() for _ in range(max(nst, n_streams))]
-            self._fws = [None] * len(self._fstreams)
-        ws_bytes = max(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])) for k in keys)
-        for i in range(nst):
-            if self._fws[i] is None or self._fws[i].numel() < ws_bytes:
-                self._fws[i] = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        sig = tuple((k, int(hessians[k].shape[0])) for k in keys)
+        if getattr(self, "_fsig", None) != sig:
+            self._fws = {k: torch.empty(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])), dtype=torch.uint8,
+                                        device="cuda") for k in keys}
+            self._fsig = sig
         status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
-        ready = torch.cuda.Event()
-        ready.record(main)
-        out, pending = {}, {}
+        out, jobs = {}, []
         for i, k in enumerate(keys):
             H = hessians[k]
             n = int(H.shape[0])
@@ -90,27 +85,23 @@ class Encoder:
             order = np.argsort(-diag) if self.act_order else np.arange(n)
             mean_diag = float(np.mean(np.asarray(diag, np.float64)[order]))
             base = mean_diag if mean_diag > 0.0 else 1.0
-            pending[k] = order
-            od = torch.from_numpy(order.astype(np.int32)).to("cuda", non_blocking=False)
+            od = torch.from_numpy(order.astype(np.int32)).to("cuda")
             U = torch.empty((n, n), dtype=torch.float32, device="cuda")
-            ut2 = torch.empty(L.cp_ef_u_bytes(n) // 4, dtype=torch.float32, device="cuda")
-            st = self._fstreams[i % nst]
-            st.wait_event(ready)
-            sp = nat.stream_ptr(torch, st)
-            ws = self._fws[i % nst]
-            nat.check(L.cp_factor_u(nat.ptr(H), n, nat.ptr(od), float(self.damp * base + 1e-8), nat.ptr(U),
-                                    nat.ptr(ws), ws.numel(), nat.ptr(status[i:i + 1]), sp), f"factor[{k}]")
-            nat.check(L.cp_ef_prepare_u(nat.ptr(U), n, nat.ptr(ut2), sp), "prepare_u")
-            out[k] = Factor(U, order, od, self.damp, ut2)
-        for i in range(nst):
-            ev = torch.cuda.Event()
-            ev.record(self._fstreams[i])
-            main.wait_event(ev)
+            jobs.append(nat.FactorJob(H.data_ptr(), n, od.data_ptr(), float(self.damp * base + 1e-8), U.data_ptr(),
+                                      self._fws[k].data_ptr(), status[i:i + 1].data_ptr()))
+            out[k] = Factor(U, order, od, self.damp)
+        arr = nat.job_array(nat.FactorJob, jobs)
+        s = nat.stream_ptr(torch, self.stream)
+        nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(jobs), s), "factor_u_batch")
+        for k in keys:
+            f = out[k]
+            f.ut2 = torch.empty(L.cp_ef_u_bytes(int(f.U.shape[0])) // 4, dtype=torch.float32, device="cuda")
+            nat.check(L.cp_ef_prepare_u(nat.ptr(f.U), int(f.U.shape[0]), nat.ptr(f.ut2), s), "prepare_u")
         st_host = status.cpu().numpy()
         for i, k in enumerate(keys):
             if st_host[i] == 0:
                 continue
-            order = pending[k]
+            order = out[k].order
             U, d = efm.factor_u_dev(hessians[k], order, damp=self.damp * 10.0, _max_tries=_max_tries - 1,
                                     diag_host=(diags or {}).get(k), stream=self.stream)
             out[k] = Factor(U, order, out[k].order_dev, d, efm.prepare_u_dev(U, stream=self.stream))
