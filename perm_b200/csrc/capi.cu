@@ -361,7 +361,7 @@ static int block_batch(int op, const cp_block_job* jobs, int count, void* stream
     d.nsb = j.nrow * d.nsb_row;
     d.sb0 = total;
     d.type = j.ggml_type;
-    total += d.nsb;
+    total += op == 2 ? (d.nsb + 15) / 16 : d.nsb;
   }
   return CP_OK;
 }

@@ -291,18 +291,25 @@ __device__ __forceinline__ void repack_sb(const SbDesc& t, int64_t sb) {
   }
 }
 
+constexpr int kWerrSbPerCta = 16;
+
+// Weighted squared error of superblocks [c*16, c*16 + 16) of one tensor, one atomic per CTA.
 template <int T>
-__device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t sb) {
+__device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t c) {
   constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
-  const uint8_t* b = t.raw + sb * block_bytes(T);
   const int i = threadIdx.x;
-  float dl, ml;
-  grid_of<T>(b, i / SW, dl, ml);
-  float v = dl * (float)code_of<T>(b, i);
-  if (!(T == kQ3_K || T == kQ6_K)) v = v - ml;
-  const float d = v - t.x[sb * 256 + i];
-  const float wt = t.w ? t.w[(sb % t.nsb_row) * 256 + i] : 1.0f;
-  double acc = (double)(d * d * wt);
+  double acc = 0.0;
+  const int64_t sb_end = min(t.nsb, (c + 1) * kWerrSbPerCta);
+  for (int64_t sb = c * kWerrSbPerCta; sb < sb_end; sb++) {
+    const uint8_t* b = t.raw + sb * block_bytes(T);
+    float dl, ml;
+    grid_of<T>(b, i / SW, dl, ml);
+    float v = dl * (float)code_of<T>(b, i);
+    if (!(T == kQ3_K || T == kQ6_K)) v = v - ml;
+    const float d = v - t.x[sb * 256 + i];
+    const float wt = t.w ? t.w[(sb % t.nsb_row) * 256 + i] : 1.0f;
+    acc += (double)(d * d * wt);
+  }
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   __shared__ double red[8];
   if ((i & 31) == 0) red[i >> 5] = acc;

@@ -52,7 +52,8 @@ struct SbBatch {
   int count;
   SbDesc d[kSbBatchMax];
 };
-// op 0: grid params, 1: repack codes, 2: weighted squared error (err must be zeroed)
+// op 0: grid params, 1: repack codes (one CTA per superblock), 2: weighted squared error
+// added to *err (one CTA per 16 superblocks; sb0 counts CTAs)
 int launch_sb_batch(int op, const SbBatch& b, int64_t total_sb, cudaStream_t stream);
 // (sub-block width, code lo, code hi, has-min) of a k-quant type; false for other types.
 bool grid_spec(int type, int* sbw, int* lo, int* hi, bool* has_min);

@@ -135,3 +135,141 @@ def ef_encode(x, ttype, qw, H, n_iter=2, damp=0.01, act_order=True):
     raw, _ = ef_encode_dev(x_dev, ttype, qw_dev, prepare_u_dev(U_dev), order, n_iter)
     recon = kq.dequantize_dev(ttype, raw, n)
     return raw.cpu().numpy(), recon.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------- driver
+
+def _hessian_to_device(torch, st, perm=None):
+    """Stored Hessian components -> float64 [d, d] on the device (hessians.py:542-560
+    arithmetic); a permutation is applied on the host first (ef.py:289-290)."""
+    from . import gguf_io
+    h = st["h"]
+    if perm is None and h.dtype == np.float16:
+        d = h.shape[0]
+        h16 = torch.from_numpy(np.ascontiguousarray(h).view(np.int16)).cuda()
+        d32 = torch.from_numpy(st["diag32"]).cuda() if st["diag32"] is not None else None
+        H = torch.empty((d, d), dtype=torch.float64, device="cuda")
+        nat.check(nat.lib().cp_hessian_decode(nat.ptr(h16), nat.ptr(d32), float(st["hscale"]), d, nat.ptr(H),
+                                              nat.stream_ptr(torch)), "hessian_decode")
+        return H
+    Hn = h.astype(np.float64)
+    if st["hscale"] != 1.0:
+        Hn *= st["hscale"]
+    if st["diag32"] is not None:
+        np.fill_diagonal(Hn, st["diag32"].astype(np.float64))
+    if perm is not None:
+        Hn = Hn[np.ix_(perm, perm)]
+    return torch.from_numpy(np.ascontiguousarray(Hn)).cuda()
+
+
+def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, perms=None, spacemap=None, dims=None,
+                acknowledge_unreviewed=False, only="all", n_iter=2, unsafe_storage_order=False, device="cuda",
+                log=print, max_params_per_batch=2_000_000_000):
+    """ef.py:223-317 on the GPU: EF-encode every quantized tensor of `target_path` with the f16
+    weights of `f16_path` and the Hessians in `hessdir`, write a clone of the target with the
+    new payloads to `out_path` and the per-tensor statistics to out_path + ".efstats.json".
+
+    Same arguments, modes ("EF", "wRTN(attn0-diag)" for token_embd, "wRTN" without a
+    Hessian), errors and outputs as the reference; tensors are encoded in device batches of
+    at most max_params_per_batch parameters and identical Hessians are factorised once."""
+    import hashlib
+    import json
+    import time
+    from gguf import GGUFReader
+    from . import gguf_io
+    from .encoder import Encoder, Job
+    if device is not None and not str(device).startswith("cuda"):
+        raise ValueError(f"perm_b200.encode_gguf runs on CUDA devices only (device={device!r})")
+    imat = gguf_io.imatrix_means(imatrix_path) if imatrix_path else {}
+    f16 = {t.name: t for t in GGUFReader(f16_path).tensors}
+    tr = GGUFReader(target_path)
+    supported = set(kq.QUANTIZE)
+    targets = [(t.name, t.tensor_type.name) for t in tr.tensors if t.tensor_type.name in supported]
+    unsupported = [(t.name, t.tensor_type.name) for t in tr.tensors
+                   if t.tensor_type.name not in supported and t.tensor_type.name not in ("F16", "F32", "BF16")]
+    if unsupported:
+        raise ValueError(f"target has types we cannot encode: {unsupported}")
+    ack = {"acknowledge_unreviewed": acknowledge_unreviewed} if acknowledge_unreviewed else {}
+    torch = nat.torch_cuda()
+    if device is not None and ":" in str(device):
+        torch.cuda.set_device(torch.device(device))
+
+    def input_perm(name):
+        if perms is None or spacemap is None:
+            return None
+        return spacemap.input_perm(name, perms, dims, **ack)
+
+    plan = []
+    for name, tt in targets:
+        is_embdout = name in ("token_embd.weight", "output.weight")
+        if (only == "blk" and is_embdout) or (only == "embdout" and not is_embdout):
+            continue
+        qw = imat.get(name)
+        p = input_perm(name)
+        if qw is not None and p is not None:
+            qw = qw[p]
+        if name == "token_embd.weight":
+            H0, n0 = gguf_io.load_hessian(hessdir, "blk.0.attn_q.weight")
+            fit_w = (np.diag(H0) / max(n0, 1)).astype(np.float32)
+            if p is not None:
+                fit_w = fit_w[p]
+            plan.append((name, tt, "wRTN(attn0-diag)", qw, None, fit_w, p))
+        elif gguf_io.has_hessian(hessdir, name):
+            if tt not in nat.K_TYPES:
+                raise ValueError(tt)  # ef.py:_grid_params supports the k-quants only
+            plan.append((name, tt, "EF" if not unsafe_storage_order else "EF(storage-order)", qw, name, None, p))
+        else:
+            plan.append((name, tt, "wRTN", qw, None, None, p))
+
+    enc = Encoder(n_iter=n_iter, act_order=not unsafe_storage_order)
+    replace, stats = {}, {}
+    t_start = time.time()
+    i = 0
+    while i < len(plan):
+        batch, total = [], 0
+        while i < len(plan) and (not batch or total + f16[plan[i][0]].n_elements <= max_params_per_batch):
+            batch.append(plan[i])
+            total += int(f16[plan[i][0]].n_elements)
+            i += 1
+        t0 = time.time()
+        hess_dev, hkey_of, diags = {}, {}, {}
+        jobs = []
+        for name, tt, mode, qw, hname, fit_w, p in batch:
+            x = torch.from_numpy(np.ascontiguousarray(np.asarray(f16[name].data).astype(np.float32))).cuda()
+            hk = None
+            if hname is not None:
+                st = gguf_io.load_hessian_stored(hessdir, hname)
+                dig = hashlib.sha1(st["h"].tobytes())
+                dig.update(np.float64(st["hscale"]).tobytes())
+                if st["diag32"] is not None:
+                    dig.update(st["diag32"].tobytes())
+                if p is not None:
+                    dig.update(np.asarray(p, np.int64).tobytes())
+                hk = dig.hexdigest()
+                if hk not in hess_dev:
+                    hess_dev[hk] = _hessian_to_device(torch, st, p)
+                    diags[hk] = torch.diagonal(hess_dev[hk]).cpu().numpy()
+            jobs.append(Job(name, tt, "EF" if mode.startswith("EF") else mode, x,
+                            None if qw is None else torch.from_numpy(np.ascontiguousarray(qw, np.float32)).cuda(),
+                            hk, None if fit_w is None else torch.from_numpy(fit_w).cuda()))
+        factors = enc.factor(hess_dev, diags)
+        raws, st = enc.encode(jobs, factors, stats=True)
+        dt = time.time() - t0
+        for (name, tt, mode, *_), j in zip(batch, jobs):
+            replace[name] = raws[name].cpu().numpy().reshape(-1)
+            s = st[name]
+            s["mode"] = mode
+            s["sec"] = dt * j.params / max(1, total)
+            stats[name] = s
+        for k, (name, tt, mode, *_) in enumerate(batch):
+            if (len(stats) - len(batch) + k + 1) % 20 == 0 or name in ("token_embd.weight", "output.weight"):
+                log(f"[{len(stats) - len(batch) + k + 1}/{len(targets)}] {name} {tt} {mode} "
+                    f"err-vs-stock {stats[name]['rel_err_vs_stock'] * 100:+.1f}% ({stats[name]['sec']:.1f}s)")
+        del jobs, raws, factors, hess_dev
+    gguf_io.copy_gguf(target_path, out_path, replace)
+    if stats:
+        med = float(np.median([s["rel_err_vs_stock"] for s in stats.values()]))
+        log(f"median err-vs-stock: {med * 100:+.2f}%; total {(time.time() - t_start) / 60:.1f} min")
+    with open(out_path + ".efstats.json", "w") as fh:
+        json.dump(stats, fh, indent=1)
+    return stats

@@ -1,0 +1,51 @@
+"""encode_gguf(device="cuda") end to end on a synthetic model: every output tensor must match
+the reference semantics (EF with its Hessian, attn0-diagonal weighted RTN for token_embd,
+weighted RTN without a Hessian), computed by the CPU oracle from the same files."""
+import json
+
+import numpy as np
+import pytest
+
+import gguf_fixtures as fx
+
+pytestmark = pytest.mark.gpu
+
+
+def test_encode_gguf_matches_reference_semantics(tmp_path, orc):
+    from gguf import GGUFReader
+    from perm_b200 import ef, gguf_io
+    W = fx.weights()
+    f16, tgt, out = str(tmp_path / "f16.gguf"), str(tmp_path / "t.gguf"), str(tmp_path / "o.gguf")
+    hdir, imp = str(tmp_path / "hess"), str(tmp_path / "im.gguf")
+    fx.write_f16(f16, W)
+    fx.write_target(tgt, W, orc.quantize)
+    gguf_io.save_hessians(fx.hessians(), hdir)
+    fx.write_imatrix(imp, [(n, ne0) for n, tt, ne0, nrow in fx.SPEC if n != "token_embd.weight"])
+    stats = ef.encode_gguf(f16, tgt, hdir, out, imatrix_path=imp, log=lambda *_: None)
+    imat = gguf_io.imatrix_means(imp)
+    got = {t.name: np.asarray(t.data) for t in GGUFReader(out).tensors}
+    for name, tt, ne0, nrow in fx.SPEC:
+        x = W[name].astype(np.float16).astype(np.float32)
+        qw = imat.get(name)
+        if name == "token_embd.weight":
+            H0, n0 = gguf_io.load_hessian(hdir, "blk.0.attn_q.weight")
+            want = orc.quantize(tt, x, (np.diag(H0) / n0).astype(np.float32))
+            assert stats[name]["mode"] == "wRTN(attn0-diag)"
+            assert np.array_equal(got[name].reshape(want.shape), want)
+        elif gguf_io.has_hessian(hdir, name):
+            H, _ = gguf_io.load_hessian(hdir, name)
+            want, _ = orc.ef_encode(x, tt, qw, H, n_iter=2, act_order=True)
+            g = got[name].reshape(want.shape)
+            frac = float(np.mean(orc.codes(tt, g, nrow, ne0) == orc.codes(tt, want, nrow, ne0)))
+            assert stats[name]["mode"] == "EF"
+            assert frac >= 0.999, f"{name}: codes identical {frac:.4%}"
+        else:
+            want = orc.quantize(tt, x, qw)
+            assert stats[name]["mode"] == "wRTN"
+            assert np.array_equal(got[name].reshape(want.shape), want)
+    assert np.array_equal(got["blk.0.attn_norm.weight"], np.ones(256, np.float32))
+    on_disk = json.load(open(out + ".efstats.json"))
+    assert set(on_disk) == {n for n, *_ in fx.SPEC}
+    assert all(np.isfinite(v["rel_err_vs_stock"]) for v in on_disk.values())
+
+
