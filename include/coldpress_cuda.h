@@ -125,6 +125,21 @@ int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const in
                 const float* u_prepared, const float* dl, const float* ml, int8_t* codes, float* w_out,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* cp_ef_sweep for callers that cannot allocate device memory.  No counterpart in the
+ * reference: it exists for hosts whose device memory is owned by another allocator (a
+ * framework's caching allocator, a serving runtime that reserves the whole GPU up front) or
+ * that reach this library through an FFI with no way to allocate or pass a scratch buffer.
+ * The sweep's working rows go to a fixed array of CP_NOALLOC_SCRATCH_BYTES inside the
+ * library, held on every GPU that loads it until the process exits; this call itself
+ * allocates nothing.  Shapes with ceil(nrow/32)*32 * n * 4 > CP_NOALLOC_SCRATCH_BYTES are
+ * rejected with CP_ERR_WORKSPACE.  The first call on a device looks the array's address up
+ * (make that call before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be serialised. */
+#define CP_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int cp_ef_sweep_noalloc(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
+                        const float* u_prepared, const float* dl, const float* ml, int8_t* codes, float* w_out,
+                        void* stream);
+
 /* ---------------------------------------------------------------- grouped calls
  * The same operations over many tensors in as few launches as possible (one per ~256 jobs),
  * so a whole model fills the GPU even where single tensors are small.  Job arrays live in

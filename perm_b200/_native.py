@@ -100,6 +100,7 @@ def lib():
         "cp_weighted_err_batch": ([P, I, P], I),
         "cp_ef_sweep_batch": ([P, I, P], I),
         "cp_factor_u_batch": ([P, I, P], I),
+        "cp_ef_sweep_noalloc": ([I, P, I64, I64, P, P, P, P, P, P, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

@@ -243,6 +243,27 @@ int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* o
                   "cp_ef_sweep");
 }
 
+int cp_ef_sweep_noalloc(int t, const float* x, int64_t nrow, int64_t n, const int32_t* order, const float* ut2,
+                        const float* dl, const float* ml, int8_t* codes, float* w_out, void* stream) {
+  if (int rc = check_shape(t, nrow, n, false)) return rc;
+  if (nrow == 0) return CP_OK;
+  int sbw, lo, hi;
+  bool hm;
+  cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
+  if (!x || !order || !ut2 || !dl || (hm && !ml) || !codes) return set_err(CP_ERR_ARG, "null pointer");
+  if (cpk::ef_sweep_workspace_bytes(nrow, n) > cpk::kNoAllocScratchBytes) {
+    std::snprintf(g_err, sizeof(g_err),
+                  "cp_ef_sweep_noalloc: ceil(nrow/32)*32 * n * 4 bytes = %zu exceeds the fixed %zu-byte scratch; "
+                  "use cp_ef_sweep with a workspace",
+                  cpk::ef_sweep_workspace_bytes(nrow, n), cpk::kNoAllocScratchBytes);
+    return CP_ERR_WORKSPACE;
+  }
+  const int rc = cpk::launch_ef_sweep_noalloc(t, x, nrow, n, order, ut2, dl, ml, codes, w_out, (cudaStream_t)stream);
+  if (rc == 4) return check_launch("cp_ef_sweep_noalloc: locating the fixed scratch");
+  if (rc == 5) return set_err(CP_ERR_ARG, "cp_ef_sweep_noalloc: device index out of range");
+  return check_rc(rc, "cp_ef_sweep_noalloc");
+}
+
 size_t cp_ef_workspace_bytes(int t, int64_t nrow, int64_t n) {
   if (!is_k_type(t) || nrow <= 0 || n <= 0) return 0;
   return ef_layout(t, nrow, n).total;

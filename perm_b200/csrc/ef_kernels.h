@@ -25,6 +25,10 @@ struct SweepBatch {
 bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* ut2,
                 const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d);
 int launch_ef_sweep_batch(const SweepBatch& b, int total_tiles, int warps, cudaStream_t stream);
+// Sweep with its working rows in a fixed per-device array (no caller workspace).
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
+int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* UT2,
+                            const float* dl, const float* ml, int8_t* codes, float* wcur, cudaStream_t stream);
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
 size_t ef_ut2_bytes(int64_t n);
 int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream);

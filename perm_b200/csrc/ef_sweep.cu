@@ -16,6 +16,7 @@
 // (coalesced float2 per lane); U is read from a column-pair-interleaved transpose
 // UT2[pair][jj][2] so one 16-byte broadcast load feeds two jj steps of a column pair.
 #include <cuda_runtime.h>
+#include <mutex>
 #include "kq_common.cuh"
 #include "kquant_kernels.h"
 #include "ef_kernels.h"
@@ -262,6 +263,47 @@ int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int
   if (!sweep_desc(type, x, nrow, n, order, UT2, dl, ml, work, codes, wcur, &b.d[0])) return 1;
   const int tiles = (int)((nrow + 31) / 32);
   return launch_ef_sweep_batch(b, tiles, tiles >= 2 * 16 * 148 ? 1 : 8, stream);
+}
+
+// ---------------------------------------------------------------------------- no-allocation sweep
+// For callers that cannot allocate device memory, the sweep can run with its working rows in
+// this fixed array instead of a caller workspace.  It is a file-scope device variable, so every
+// GPU that loads the library reserves it until the process exits.  Host code must not use the
+// name g_noalloc_scratch as an address: on the host it is only a stand-in for the symbol, so
+// the device address is looked up once per device with cudaGetSymbolAddress.  All calls share
+// the array (the last call's contents stay in it), so calls that overlap on the GPU race.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+constexpr int kMaxNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxNoAllocDevices] = {};
+}  // namespace
+
+// Device address of the scratch array on the current device; looked up on the first call per
+// device (which must therefore not happen during a stream capture).
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 4;
+  if (dev < 0 || dev >= kMaxNoAllocDevices) return 5;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return 4;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return 0;
+}
+
+int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* UT2,
+                            const float* dl, const float* ml, int8_t* codes, float* wcur, cudaStream_t stream) {
+  if (ef_sweep_workspace_bytes(nrow, n) > kNoAllocScratchBytes) return 6;
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // The sweep writes every working element of its tiles before reading it, so the array's
+  // previous contents need no clearing.
+  return launch_ef_sweep(type, x, nrow, n, order, UT2, UT2 + (size_t)n * n, dl, ml, scratch, codes, wcur, stream);
 }
 
 }  // namespace cpk
