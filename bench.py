@@ -299,8 +299,8 @@ def gpu_arm(args, rank, world, local_rank):
     enc = Encoder(n_iter=2, damp=0.01, act_order=True)
 
     def step():
-        factors = enc.factor({k: wl.hess[k] for k in wl.ef_keys}, {k: wl.diags[k] for k in wl.ef_keys})
-        _, st = enc.encode(jobs, factors, stats=True, outputs=outputs)
+        _, st = enc.run(jobs, {k: wl.hess[k] for k in wl.ef_keys}, {k: wl.diags[k] for k in wl.ef_keys},
+                        stats=True, outputs=outputs)
         if world > 1:
             gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
         return st
@@ -440,11 +440,11 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
             dev_w16[j.name].copy_(host_w[j.name], non_blocking=True)
             j.x.copy_(dev_w16[j.name])
         hs = {k: dev_h[k][2] for k in wl.ef_keys}
-        factors = enc.factor(hs, None)
+        diags = {k: torch.diagonal(h).cpu().numpy() for k, h in hs.items()}
         for j in jobs:
             if j.qw is not None:
                 j.qw.copy_(torch.diagonal(hs[j.hkey]).float())
-        enc.encode(jobs, factors, stats=True, outputs=outputs)
+        enc.run(jobs, hs, diags, stats=True, outputs=outputs)
         if world > 1:
             bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
             if rank == 0:

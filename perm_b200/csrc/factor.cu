@@ -16,6 +16,17 @@
 namespace cpk {
 
 constexpr int NB = 64;
+constexpr int kSplitMax = 16;
+
+// K splitting of the long products: chunks of about 256 (a multiple of 16), at most 16.
+__host__ __device__ inline int ksplit(int K) {
+  if (K <= 384) return 1;
+  const int s = (K + 255) / 256;
+  return s > kSplitMax ? kSplitMax : s;
+}
+__host__ __device__ inline int kchunk(int K, int S) { return ((K + S - 1) / S + 15) / 16 * 16; }
+// partial tiles live after P (n x n) and T (n x 64) in each item's workspace
+__device__ __forceinline__ double* part_base(double* P, int n) { return P + (size_t)n * n + (size_t)n * NB; }
 
 // P[i][j] = H[order[n-1-i]][order[n-1-j]] (+ shift on the diagonal).  Only the lower
 // triangle is consumed; the strict upper triangle is written as zero.  blockIdx.z: item.
@@ -39,17 +50,24 @@ __global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
 // column and updates the trailing triangle element-parallel; each inverse column step forms
 // the row dot products with four threads per row and a shuffle reduction.
 // A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
-__global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k) {
+__global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k, int S) {
   __shared__ double a[NB][NB + 1];
   __shared__ double piv[NB];
   const int t = threadIdx.x;
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.x];
+  const double* part = part_base(A, n);
   int* status = fb.status[blockIdx.x];
   if (*status) return;
   for (int i = t; i < NB * NB; i += 256) {
     const int r = i / NB, c = i % NB;
-    a[r][c] = (c <= r) ? A[(size_t)(k + r) * n + k + c] : 0.0;
+    double v = 0.0;
+    if (c <= r) {
+      v = A[(size_t)(k + r) * n + k + c];
+      if (S > 1)  // split update of this column block: subtract its partial products in order
+        for (int q = 0; q < S; q++) v -= part[((size_t)q * n + k + r) * NB + c];
+    }
+    a[r][c] = v;
   }
   __syncthreads();
   for (int j = 0; j < NB; j++) {
@@ -170,29 +188,50 @@ __device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, co
 
 // Left-looking Cholesky step j, before the diagonal factorisation:
 //   A[j:n, j:j+64] -= L[j:n, 0:j] * L[j:j+64, 0:j]^T        (one 64-row tile per CTA)
-__global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j) {
+// With S > 1 the K range is split over blockIdx.y and each CTA writes its partial product;
+// the diagonal kernel and the panel solve subtract the partials (in order) when they read.
+__global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
-  double* __restrict__ A = fb.P[blockIdx.y];
-  if (*fb.status[blockIdx.y]) return;
+  double* __restrict__ A = fb.P[blockIdx.z];
+  if (*fb.status[blockIdx.z]) return;
   const int r0 = j + blockIdx.x * 64;
+  const int q = blockIdx.y, chunk = kchunk(j, S);
+  const int k0 = q * chunk, k1 = min(j, k0 + chunk);
   double acc[8][8];
-  tile64<true>(A + (size_t)r0 * n, n, A + (size_t)j * n, n, n - r0, 64, j, acc);
+  tile64<true>(A + (size_t)r0 * n + k0, n, A + (size_t)j * n + k0, n, n - r0, 64, k1 - k0, acc);
   const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
+  double* part = part_base(A, n) + (size_t)q * n * NB;
 #pragma unroll
   for (int r = 0; r < 8; r++)
 #pragma unroll
     for (int c = 0; c < 8; c++) {
-      const int rr = r0 + tm + 8 * r, cc = j + tn + 8 * c;
-      if (rr < n && rr >= cc) A[(size_t)rr * n + cc] -= acc[r][c];
+      const int rr = r0 + tm + 8 * r, cc = tn + 8 * c;
+      if (rr >= n) continue;
+      if (S == 1) {
+        if (rr >= j + cc) A[(size_t)rr * n + j + cc] -= acc[r][c];
+      } else {
+        part[(size_t)rr * NB + cc] = acc[r][c];
+      }
     }
 }
 
 // Panel below the diagonal block: A[j+64:n, j:j+64] := A * inv(L_jj)^T (inverse on the diagonal).
-__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
+__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
   if (*fb.status[blockIdx.y]) return;
   const int r0 = j + 64 + blockIdx.x * 64;
+  if (S > 1) {  // finish this tile's split update before solving with it
+    const double* part = part_base(A, n);
+    for (int i = threadIdx.x; i < 64 * 64; i += 64) {
+      const int rr = r0 + i / 64, c = i % 64;
+      if (rr >= n) continue;
+      double v = A[(size_t)rr * n + j + c];
+      for (int q = 0; q < S; q++) v -= part[((size_t)q * n + rr) * NB + c];
+      A[(size_t)rr * n + j + c] = v;
+    }
+    __syncthreads();
+  }
   double acc[8][8];
   tile64<true>(A + (size_t)r0 * n + j, n, A + (size_t)j * n + j, n, n - r0, 64, 64, acc);
   __syncthreads();  // every CTA reads only its own rows of the panel, so in-place is safe
@@ -208,36 +247,55 @@ __global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ 
 
 // Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
 //   T = -Linv22 * L21          (rows below, into scratch; Linv22 is lower triangular)
-__global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ FactorBatch fb, int j) {
+// With S > 1 the K range is split over blockIdx.y; partial products go to the partial-tile
+// scratch and trinv_apply forms T from them in order.
+__global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
-  const double* __restrict__ A = fb.P[blockIdx.y];
-  double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
-  if (*fb.status[blockIdx.y]) return;
+  double* __restrict__ Pw = fb.P[blockIdx.z];
+  const double* __restrict__ A = Pw;
+  double* __restrict__ T = Pw + (size_t)n * n;
+  if (*fb.status[blockIdx.z]) return;
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
   const int k_len = r0 + m - base;  // rows r0.. of Linv22 vanish right of column r0+m-1
+  const int q = blockIdx.y, chunk = kchunk(n - base, S);
+  const int k0 = q * chunk, k1 = min(k_len, k0 + chunk);
   double acc[8][8];
-  tile64<false>(A + (size_t)r0 * n + base, n, A + (size_t)base * n + j, n, m, 64, k_len, acc);
+  tile64<false>(A + (size_t)r0 * n + base + k0, n, A + (size_t)(base + k0) * n + j, n, m, 64, k1 - k0, acc);
   const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
+  double* part = part_base(Pw, n) + (size_t)q * n * NB;
 #pragma unroll
   for (int r = 0; r < 8; r++)
 #pragma unroll
     for (int c = 0; c < 8; c++) {
       const int rr = tm + 8 * r;
-      if (rr < m) T[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = -acc[r][c];
+      if (rr >= m) continue;
+      if (S == 1) T[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = -acc[r][c];
+      else part[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = acc[r][c];
     }
 }
 
 //   L21 := T * inv(L_jj)   (inv(L_jj) already sits on the diagonal)
-__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
+__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
-  const double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
+  double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
   if (*fb.status[blockIdx.y]) return;
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
+  if (S > 1) {  // T rows of this tile = -(sum of the split partial products, in order)
+    const double* part = part_base(A, n);
+    for (int i = threadIdx.x; i < 64 * 64; i += 64) {
+      const int rr = i / 64, c = i % 64;
+      if (rr >= m) continue;
+      double v = 0.0;
+      for (int q = 0; q < S; q++) v += part[((size_t)q * n + r0 - base + rr) * NB + c];
+      T[(size_t)(r0 - base + rr) * NB + c] = -v;
+    }
+    __syncthreads();
+  }
   double acc[8][8];
   tile64<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, 64, 64, acc);
   const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
@@ -262,8 +320,8 @@ __global__ void unreverse_cast_kernel(const __grid_constant__ FactorBatch fb) {
 }
 
 size_t factor_workspace_bytes(int64_t n) {
-  // P (n x n f64) + T (n x nb)
-  return ((size_t)n * n + (size_t)n * NB) * sizeof(double);
+  // P (n x n f64) + T (n x nb) + split-K partial tiles (kSplitMax x n x nb)
+  return ((size_t)n * n + (size_t)n * NB + (size_t)kSplitMax * n * NB) * sizeof(double);
 }
 
 int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
@@ -277,14 +335,15 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     note_launch();
   }
   for (int j = 0; j < n; j += NB) {
+    const int S = j > 0 ? ksplit(j) : 1;
     if (j > 0) {
-      chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
+      chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
       note_launch();
     }
-    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j);
+    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j, S);
     note_launch();
     if (n - j - NB > 0) {
-      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
+      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
       note_launch();
     }
   }
@@ -292,9 +351,10 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   // blocks were inverted by the factorisation
   for (int j = n - 2 * NB; j >= 0; j -= NB) {
     const unsigned tiles = (unsigned)((n - j - NB + 63) / 64);
-    trmm_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
+    const int S = ksplit(n - j - NB);
+    trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
     note_launch();
-    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
+    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
     note_launch();
   }
   {

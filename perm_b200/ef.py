@@ -252,8 +252,7 @@ def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, per
             jobs.append(Job(name, tt, "EF" if mode.startswith("EF") else mode, x,
                             None if qw is None else torch.from_numpy(np.ascontiguousarray(qw, np.float32)).cuda(),
                             hk, None if fit_w is None else torch.from_numpy(fit_w).cuda()))
-        factors = enc.factor(hess_dev, diags)
-        raws, st = enc.encode(jobs, factors, stats=True)
+        raws, st = enc.run(jobs, hess_dev, diags, stats=True)
         dt = time.time() - t0
         for (name, tt, mode, *_), j in zip(batch, jobs):
             replace[name] = raws[name].cpu().numpy().reshape(-1)
@@ -265,7 +264,7 @@ def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, per
             if (len(stats) - len(batch) + k + 1) % 20 == 0 or name in ("token_embd.weight", "output.weight"):
                 log(f"[{len(stats) - len(batch) + k + 1}/{len(targets)}] {name} {tt} {mode} "
                     f"err-vs-stock {stats[name]['rel_err_vs_stock'] * 100:+.1f}% ({stats[name]['sec']:.1f}s)")
-        del jobs, raws, factors, hess_dev
+        del jobs, raws, hess_dev
     gguf_io.copy_gguf(target_path, out_path, replace)
     if stats:
         med = float(np.median([s["rel_err_vs_stock"] for s in stats.values()]))

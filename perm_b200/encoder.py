@@ -60,7 +60,7 @@ class Encoder:
         self._fstreams = None
 
     # ---------------------------------------------------------------- factorisation
-    def factor(self, hessians, diags=None, _max_tries=6):
+    def factor(self, hessians, diags=None, _max_tries=6, check=True):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
         Returns {key: Factor}.  All first attempts go out as one batched call (same-size
         Hessians advance through each factorisation step in a single launch); the status
@@ -90,22 +90,66 @@ class Encoder:
             jobs.append(nat.FactorJob(H.data_ptr(), n, od.data_ptr(), float(self.damp * base + 1e-8), U.data_ptr(),
                                       self._fws[k].data_ptr(), status[i:i + 1].data_ptr()))
             out[k] = Factor(U, order, od, self.damp)
-        arr = nat.job_array(nat.FactorJob, jobs)
-        s = nat.stream_ptr(torch, self.stream)
-        nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(jobs), s), "factor_u_batch")
+        # each size group is one chain of batched steps; the groups run side by side
+        main = self.stream if self.stream is not None else torch.cuda.current_stream()
+        sizes = sorted({int(hessians[k].shape[0]) for k in keys}, reverse=True)
+        if getattr(self, "_fstreams", None) is None or len(self._fstreams) < len(sizes):
+            self._fstreams = [torch.cuda.Stream() for _ in range(max(4, len(sizes)))]
         for k in keys:
             f = out[k]
             f.ut2 = torch.empty(L.cp_ef_u_bytes(int(f.U.shape[0])) // 4, dtype=torch.float32, device="cuda")
-            nat.check(L.cp_ef_prepare_u(nat.ptr(f.U), int(f.U.shape[0]), nat.ptr(f.ut2), s), "prepare_u")
+        ready = torch.cuda.Event()
+        ready.record(main)
+        self._factor_done = []
+        for gi, n in enumerate(sizes):
+            st = self._fstreams[gi]
+            st.wait_event(ready)
+            sp = nat.stream_ptr(torch, st)
+            grp = [(i, k) for i, k in enumerate(keys) if int(hessians[k].shape[0]) == n]
+            arr = nat.job_array(nat.FactorJob, [jobs[i] for i, _ in grp])
+            nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
+            for _, k in grp:
+                nat.check(L.cp_ef_prepare_u(nat.ptr(out[k].U), n, nat.ptr(out[k].ut2), sp), "prepare_u")
+            done = torch.cuda.Event()
+            done.record(st)
+            self._factor_done.append(done)
+            if check:
+                main.wait_event(done)
+        self._pending = (keys, status, hessians, diags, _max_tries)
+        if check:
+            self.escalate(out)
+        return out
+
+    def escalate(self, factors):
+        """Read the status words of the last factor() call (one synchronisation) and redo, with
+        the reference's damp escalation, every factorisation that hit a non-positive pivot.
+        Returns the keys whose factors changed."""
+        keys, status, hessians, diags, max_tries = self._pending
         st_host = status.cpu().numpy()
+        redone = []
         for i, k in enumerate(keys):
             if st_host[i] == 0:
                 continue
-            order = out[k].order
-            U, d = efm.factor_u_dev(hessians[k], order, damp=self.damp * 10.0, _max_tries=_max_tries - 1,
+            order = factors[k].order
+            U, d = efm.factor_u_dev(hessians[k], order, damp=self.damp * 10.0, _max_tries=max_tries - 1,
                                     diag_host=(diags or {}).get(k), stream=self.stream)
-            out[k] = Factor(U, order, out[k].order_dev, d, efm.prepare_u_dev(U, stream=self.stream))
-        return out
+            factors[k] = Factor(U, order, factors[k].order_dev, d, efm.prepare_u_dev(U, stream=self.stream))
+            redone.append(k)
+        return redone
+
+    def run(self, jobs, hessians, diags=None, stats=True, outputs=None):
+        """factor() + encode() with the factorisations overlapped with the round-1 fits: the
+        factor chains start on side streams, the fits (which need no U) go first on this
+        stream, and the status words are read once at the end; tensors whose Hessian needed
+        damp escalation are encoded again with the escalated factor."""
+        factors = self.factor(hessians, diags, check=False)
+        raws, st = self.encode(jobs, factors, stats=stats, outputs=outputs, factor_event=self._factor_done)
+        redone = set(self.escalate(factors))
+        if redone:
+            again = [j for j in jobs if j.mode == "EF" and j.hkey in redone]
+            r2, s2 = self.encode(again, factors, stats=stats, outputs={j.name: raws[j.name] for j in again})
+            st.update(s2)
+        return raws, st
 
     # ---------------------------------------------------------------- tensors
     def _arena(self, jobs):
@@ -158,7 +202,7 @@ class Encoder:
         self._arena_key, self._arena_views = key, views
         return views
 
-    def encode(self, jobs, factors, stats=True, outputs=None):
+    def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None):
         """Encode every job with grouped launches; returns ({name: raw uint8 on device},
         {name: stats dict})."""
         torch = self.torch
@@ -218,6 +262,10 @@ class Encoder:
             block_call(L.cp_weighted_err_batch,
                        werr_items([i for i, j in enumerate(jobs) if j.mode == "wRTN(attn0-diag)"], 1, True),
                        "weighted_err_batch")
+        if factor_event:  # the factorisations ran on side streams; the sweeps need them
+            main = self.stream if self.stream is not None else torch.cuda.current_stream()
+            for ev in factor_event:
+                main.wait_event(ev)
         for it in range(self.n_iter):
             if it > 0:
                 fit_batch([(jobs[i].ttype, views[i]["wcur"].view(jobs[i].x.shape), jobs[i].qw, raws[i])
@@ -231,7 +279,7 @@ class Encoder:
                                          int(j.x.shape[0]), int(j.x.shape[1])))
             block_call(L.cp_grid_params_batch, grid, "grid_params_batch")
             sw = []
-            for i in ef_idx:
+            for i in sorted(ef_idx, key=lambda i: -int(jobs[i].x.shape[1])):  # longest tiles first
                 j = jobs[i]
                 f = factors[j.hkey]
                 hm = nat.GRID[j.ttype][3]

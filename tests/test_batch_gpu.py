@@ -66,3 +66,32 @@ def test_grouped_stats_match_reference_formula(orc):
     e_ours = float(((((recon - W) ** 2) * qw).astype(np.float64)).sum())
     e_base = float(((((base - W) ** 2) * qw).astype(np.float64)).sum())
     assert abs(st["w"]["rel_err_vs_stock"] - (e_ours / e_base - 1)) < 1e-6
+
+
+def test_run_escalates_damp_for_an_indefinite_hessian(orc):
+    """Encoder.run overlaps the factorisations with the first fits and reads the status words
+    at the end; a Hessian with a clearly negative eigenvalue must be re-factorised with the
+    reference's escalated damping and its tensor re-encoded, matching the oracle."""
+    import torch
+    from perm_b200.encoder import Encoder, Job
+    rng = np.random.default_rng(4)
+    n = 256
+    Q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+    eig = np.linspace(1.0, 100.0, n)
+    eig[0] = -2.0
+    Hbad = (Q * eig) @ Q.T
+    Hbad = (Hbad + Hbad.T) / 2
+    Hgood = _hessian(rng, n)
+    W1 = (rng.standard_normal((64, n)) * 0.02).astype(np.float32)
+    W2 = (rng.standard_normal((48, n)) * 0.02).astype(np.float32)
+    q1 = np.abs(np.diag(Hbad)).astype(np.float32)
+    q2 = np.diag(Hgood).astype(np.float32)
+    jobs = [Job("bad", "Q4_K", "EF", torch.from_numpy(W1).cuda(), torch.from_numpy(q1).cuda(), "bad"),
+            Job("good", "Q2_K", "EF", torch.from_numpy(W2).cuda(), torch.from_numpy(q2).cuda(), "good")]
+    hs = {"bad": torch.from_numpy(Hbad).cuda(), "good": torch.from_numpy(Hgood).cuda()}
+    raws, st = Encoder().run(jobs, hs, {"bad": np.diag(Hbad), "good": np.diag(Hgood)})
+    for name, tt, W, qw, H in (("bad", "Q4_K", W1, q1, Hbad), ("good", "Q2_K", W2, q2, Hgood)):
+        want, _ = orc.ef_encode(W, tt, qw, H, n_iter=2, act_order=True)
+        got = raws[name].cpu().numpy()
+        frac = float(np.mean(orc.codes(tt, got, *W.shape) == orc.codes(tt, want, *W.shape)))
+        assert frac >= 0.999, f"{name}: codes identical {frac:.4%}"
