@@ -34,6 +34,7 @@ extern "C" {
 #define CP_ERR_CUDA 4      /* a CUDA launch or call failed; see cp_last_error() */
 #define CP_ERR_ARG 5       /* null pointer or out-of-range argument */
 #define CP_ERR_WORKSPACE 6 /* workspace smaller than the matching *_workspace_bytes() */
+#define CP_ERR_TIMEOUT 7   /* a kernel's bounded wait ran out (cp_xtx_status) */
 
 /* Library version (major*10000 + minor*100 + patch) and the last error message of the
  * calling thread. */
@@ -198,9 +199,27 @@ typedef struct {
  * one launch (up to 64 per launch). */
 int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream);
 
-/* hessians.py:455-470 hook arithmetic: H += x^T x for x bf16 [T, d] (row-major, d a
- * multiple of 128), H float32 [d, d], accumulated in float32 on the tensor cores. */
-int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream);
+/* Activation element types of cp_xtx_*. */
+#define CP_XTX_BF16 0
+#define CP_XTX_F32 1
+
+/* Device workspace that cp_xtx_accumulate needs for x of `dtype` [T, d] on the current
+ * device: a status word, per-tile counters, token-split partial tiles and, for float32
+ * input, the hi/lo bf16 copies of x.  Zero-fill it once when it is allocated. */
+size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d);
+
+/* hessians.py:455-470 hook arithmetic (`x.float(); acc += x.T @ x`): H += x^T x for x
+ * [T, d] row-major (bf16, or float32 split exactly into hi + lo bf16 with a 2^-17 relative
+ * remainder), H float32 [d, d] row-major, d a multiple of 8, accumulated in float32 on the
+ * tensor cores.  H stays exactly symmetric and repeated calls give identical bits.  One
+ * workspace serves one stream at a time. */
+int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, void* workspace,
+                      size_t ws_bytes, void* stream);
+
+/* Synchronises `stream`, reads and clears the workspace status word: CP_OK, or
+ * CP_ERR_TIMEOUT when a wait inside an earlier cp_xtx_accumulate ran out (its H is then
+ * incomplete). */
+int cp_xtx_status(void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

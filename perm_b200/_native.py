@@ -11,7 +11,8 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcoldpress_cuda.so")
 
-CP_OK, CP_ERR_TYPE, CP_ERR_SHAPE, CP_ERR_NOT_PD, CP_ERR_CUDA, CP_ERR_ARG, CP_ERR_WORKSPACE = range(7)
+CP_OK, CP_ERR_TYPE, CP_ERR_SHAPE, CP_ERR_NOT_PD, CP_ERR_CUDA, CP_ERR_ARG, CP_ERR_WORKSPACE, CP_ERR_TIMEOUT = range(8)
+CP_XTX_BF16, CP_XTX_F32 = 0, 1
 
 TYPE_ID = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
 K_TYPES = ("Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K")
@@ -93,7 +94,9 @@ def lib():
         "cp_ef_sweep": ([I, P, I64, I64, P, P, P, P, P, P, P, SZ, P], I),
         "cp_ef_workspace_bytes": ([I, I64, I64], SZ),
         "cp_ef_encode": ([I, P, I64, I64, P, P, P, I, P, P, P, SZ, P], I),
-        "cp_xtx_accumulate": ([P, I64, I64, P, P], I),
+        "cp_xtx_workspace_bytes": ([I, I64, I64], SZ),
+        "cp_xtx_accumulate": ([I, P, I64, I64, P, P, SZ, P], I),
+        "cp_xtx_status": ([P, P], I),
         "cp_kquant_encode_batch": ([I, P, I, P], I),
         "cp_grid_params_batch": ([P, I, P], I),
         "cp_kquant_repack_batch": ([P, I, P], I),

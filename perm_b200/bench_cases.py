@@ -5,7 +5,8 @@ on the device and runs its kernels a few times.
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
     fit      Q2_K imatrix fit of a 4096 x 4096 tensor
     factor   batched FP64 factorisation of 16 Hessians n = 1024 and 4 of n = 3072
-    xtx      X^T X of 32768 bf16 tokens at d = 1024 and d = 3072
+    xtx      X^T X of 32768 bf16 tokens at d = 1024, 2048, 3072 (tcgen05 kernel)
+    xtx_f32  the same with float32 tokens (hi/lo bf16 split, four products)
 """
 import sys
 import time
@@ -80,11 +81,22 @@ def case_factor(torch, reps):
     return f"factor 16x1024 + 4x3072: {dt * 1e3:.2f} ms, {fl / dt / 1e12:.2f} FP64 TFLOP/s"
 
 
-def case_xtx(torch, reps):
+def _xtx_tile_flops(T, d):
+    """Flops the tensor cores execute: 128 x 256 tiles on or below the diagonal."""
+    nt = -(-d // 128)
+    tiles = sum(ti // 2 + 1 for ti in range(nt))
+    return 2.0 * tiles * 128 * 256 * T
+
+
+def case_xtx(torch, reps, dtype="bf16"):
     from . import hessians
     out = []
-    for d in (1024, 3072):
-        X = (torch.randn(32768, d, device="cuda")).to(torch.bfloat16)
+    T = 32768
+    for d in (1024, 2048, 3072):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(d)
+        X = torch.randn(T, d, device="cuda", generator=g) * torch.exp(torch.randn(d, device="cuda", generator=g))
+        X = X.to(torch.bfloat16) if dtype == "bf16" else X
         H = torch.zeros(d, d, device="cuda")
         hessians.xtx_accumulate(X, H)
         torch.cuda.synchronize()
@@ -94,12 +106,19 @@ def case_xtx(torch, reps):
             hessians.xtx_accumulate(X, H)
         e.record()
         torch.cuda.synchronize()
+        hessians.xtx_status()
         ms = s.elapsed_time(e) / reps
-        out.append(f"xtx T=32768 d={d}: {ms:.3f} ms, {2 * 32768 * d * d / ms / 1e9:.1f} TFLOP/s")
+        mult = 4 if dtype == "f32" else 1
+        out.append(f"xtx {dtype} T={T} d={d}: {ms:.3f} ms, {2 * T * d * d / ms / 1e9:.1f} TFLOP/s (x^T x), "
+                   f"{mult * _xtx_tile_flops(T, d) / ms / 1e9:.1f} TFLOP/s on the tensor cores")
     return "; ".join(out)
 
 
-CASES = {"sweep": case_sweep, "fit": case_fit, "factor": case_factor, "xtx": case_xtx}
+def case_xtx_f32(torch, reps):
+    return case_xtx(torch, reps, "f32")
+
+
+CASES = {"sweep": case_sweep, "fit": case_fit, "factor": case_factor, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):

@@ -470,12 +470,48 @@ int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream) {
   return CP_OK;
 }
 
-int cp_xtx_accumulate(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, void* stream) {
-  if (T < 0 || d <= 0 || d % 128) return set_err(CP_ERR_SHAPE, "d must be a positive multiple of 128");
+static int num_sms_current() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d) {
+  if (T < 0 || d <= 0 || (dtype != CP_XTX_BF16 && dtype != CP_XTX_F32)) return 0;
+  return cpk::xtx_plan(T, d, dtype == CP_XTX_F32, num_sms_current()).ws_bytes;
+}
+
+int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, void* workspace, size_t ws_bytes,
+                      void* stream) {
+  if (dtype != CP_XTX_BF16 && dtype != CP_XTX_F32) return set_err(CP_ERR_TYPE, "dtype must be CP_XTX_BF16 or CP_XTX_F32");
+  if (T < 0 || d <= 0 || d % 8) return set_err(CP_ERR_SHAPE, "d must be a positive multiple of 8");
+  if (d > (1 << 30) || T > (int64_t)1 << 30) return set_err(CP_ERR_SHAPE, "T or d too large");
   if (T == 0) return CP_OK;
-  if (!x_bf16 || !H) return set_err(CP_ERR_ARG, "null pointer");
-  if (((uintptr_t)x_bf16 | (uintptr_t)H) & 15) return set_err(CP_ERR_ARG, "x and H must be 16-byte aligned");
-  return check_rc(cpk::launch_xtx(x_bf16, T, d, H, (cudaStream_t)stream), "cp_xtx_accumulate");
+  if (!x || !H || !workspace) return set_err(CP_ERR_ARG, "null pointer");
+  if (((uintptr_t)x | (uintptr_t)H | (uintptr_t)workspace) & 15)
+    return set_err(CP_ERR_ARG, "x, H and workspace must be 16-byte aligned");
+  const cpk::XtxPlan p = cpk::xtx_plan(T, d, dtype == CP_XTX_F32, num_sms_current());
+  if (ws_bytes < p.ws_bytes) return set_err(CP_ERR_WORKSPACE, "workspace smaller than cp_xtx_workspace_bytes()");
+  cudaStream_t s = (cudaStream_t)stream;
+  ProfScope ps(kProfOther, s);
+  const int rc = cpk::launch_xtx(x, dtype == CP_XTX_F32, T, d, H, workspace, p, s);
+  if (rc == 1) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: kernel attribute or memset failed");
+  if (rc == 2) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: cuTensorMapEncodeTiled unavailable from the driver");
+  if (rc == 3) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: cuTensorMapEncodeTiled rejected the activation layout");
+  return check_launch("cp_xtx_accumulate");
+}
+
+int cp_xtx_status(void* workspace, void* stream) {
+  if (!workspace) return set_err(CP_ERR_ARG, "null pointer");
+  int st = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(&st, workspace, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("cp_xtx_status");
+  if (st == 0) return CP_OK;
+  if (cudaMemsetAsync(workspace, 0, 4, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("cp_xtx_status");
+  return set_err(CP_ERR_TIMEOUT, "a bounded wait in cp_xtx_accumulate ran out; H is incomplete");
 }
 
 }  // extern "C"

@@ -1,8 +1,24 @@
 // Internal launcher declarations for X^T X accumulation.
 #pragma once
+#include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 namespace cpk {
-int launch_xtx(const uint16_t* x_bf16, int64_t T, int64_t d, float* H, cudaStream_t stream);
+
+// Launch shape and workspace layout of one X^T X call (all offsets in bytes).
+struct XtxPlan {
+  int nt;               // 128-wide blocks of d
+  int tiles;            // 128 x 256 tiles on or below the diagonal
+  int phases;           // 1 (bf16 input) or 4 (float32 input split into hi/lo bf16)
+  int ki;               // 64-token steps per phase
+  int splits;           // token splits
+  int steps_per_split;
+  size_t off_counters, off_partial, off_hi, off_lo, ws_bytes;
+};
+
+XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms);
+int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, void* ws, const XtxPlan& p,
+               cudaStream_t stream);
+
 }  // namespace cpk
