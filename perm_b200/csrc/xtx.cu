@@ -20,11 +20,14 @@
 // (the strict upper part comes from the mirror), so H stays exactly symmetric; sub-blocks
 // above the diagonal are dropped.
 //
+// Write-out.  After the last chunk the tile is staged row-major in the (now idle) TMA ring in
+// shared memory, so that both H[i, j] and the mirror H[j, i] are updated with coalesced
+// 128-byte row segments, loads batched ahead of stores.
+//
 // Token splits.  When there are too few tiles to fill the SMs, tokens are cut into S splits
-// of whole 64-token steps.  Each split CTA writes its f32 partial tile to the workspace and
-// bumps a per-tile counter; the CTA that arrives last sums the S partials in split order
-// 0..S-1 and adds the sum to H.  The result does not depend on which CTA came last, so
-// repeated runs give identical bits.  No CTA waits for another.
+// of whole 64-token steps.  Each split CTA writes its f32 partial tile to the workspace; a
+// second kernel sums the S partials of each tile in split order 0..S-1 and adds the sum to H
+// the same way.  Repeated runs give identical bits and no CTA waits for another.
 //
 // float32 activations.  The reference casts activations to float32 before the product and
 // small teachers run in float32.  For those inputs X is first split into two bf16 arrays,
@@ -62,6 +65,7 @@ constexpr uint32_t kTmemCols = 2 * kBN;              // two accumulators (double
 constexpr int kPartialFloats = kBM * kBN;            // 128 KB per (tile, split) partial
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+constexpr int kReduceSmem = kBM * (kBN + 1) * 4;   // staged tile, 131.6 KB
 
 // UMMA instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12
 // = 1), both MN-major (bits 15, 16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -74,7 +78,6 @@ struct XtxParams {
   int ki;            // 64-token steps per phase
   int steps_per_split;
   float* partial;    // [splits][tiles][2][4][128][32] when splits > 1
-  int* counters;     // [tiles]
   int* status;       // sticky error word
 };
 
@@ -185,32 +188,50 @@ __device__ __forceinline__ void tile_coords(int tile, int& ti, int& p) {
   p = t;
 }
 
-// Adds 32 values of row i, columns j0 .. j0+31 of one 128 x 128 sub-block (ti, tj) to H and
-// to the mirrored H[j, i].  Diagonal sub-blocks keep j <= i (direct) and j < i (mirror).
-__device__ __forceinline__ void apply32(float* __restrict__ H, int d, int i, int j0, bool diag, const float (&v)[32]) {
-  if (i >= d) return;
-  if (!diag && j0 + 32 <= d) {
-    float4* row = reinterpret_cast<float4*>(H + (size_t)i * d + j0);
+// Adds a staged 128 x 256 tile (shared memory, row pitch `pitch` floats, columns 0-127 =
+// sub-block 2tp, 128-255 = sub-block 2tp+1) to H[i, j] and to the mirror H[j, i].  Sub-blocks
+// above the diagonal or past d are skipped; a diagonal sub-block adds j <= i directly and
+// j < i mirrored, so H stays exactly symmetric.  kEpiWarps warps cooperate; every warp-wide
+// access is a 128-byte row segment, and each group of 8 loads is issued before its stores.
+__device__ __forceinline__ void add_tile_to_h(float* __restrict__ H, int d, int ti, int tp, int nt,
+                                              const float* tile_s, int pitch, int warp_id, int lane) {
+  const int i0 = ti * kBM;
+#pragma unroll 1
+  for (int hh = 0; hh < 2; hh++) {
+    const int tj = 2 * tp + hh;
+    if (tj > ti || tj >= nt) continue;
+    const bool diag = tj == ti;
+    const int j0 = tj * kBM;
+    // direct: 128 rows x 4 column chunks = 512 row segments, 64 per warp, 8 loads in flight
+#pragma unroll 1
+    for (int base_seg = warp_id; base_seg < kBM * 4; base_seg += 8 * kEpiWarps) {
+      float h[8];
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      float4 h = row[q];
-      h.x += v[4 * q];
-      h.y += v[4 * q + 1];
-      h.z += v[4 * q + 2];
-      h.w += v[4 * q + 3];
-      row[q] = h;
+      for (int k = 0; k < 8; k++) {
+        const int seg = base_seg + k * kEpiWarps, r = seg >> 2, j = j0 + (seg & 3) * 32 + lane, i = i0 + r;
+        h[k] = (i < d && j < d && (!diag || j <= i)) ? H[(size_t)i * d + j] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int seg = base_seg + k * kEpiWarps, r = seg >> 2, c = (seg & 3) * 32 + lane, j = j0 + c, i = i0 + r;
+        if (i < d && j < d && (!diag || j <= i)) H[(size_t)i * d + j] = h[k] + tile_s[r * pitch + hh * 128 + c];
+      }
     }
-  } else {
+    // mirror: 128 columns x 4 row groups of 32, lanes over rows
+#pragma unroll 1
+    for (int base_seg = warp_id; base_seg < kBM * 4; base_seg += 8 * kEpiWarps) {
+      float h[8];
 #pragma unroll
-    for (int e = 0; e < 32; e++) {
-      const int j = j0 + e;
-      if (j < d && (!diag || j <= i)) H[(size_t)i * d + j] += v[e];
+      for (int k = 0; k < 8; k++) {
+        const int seg = base_seg + k * kEpiWarps, c = seg >> 2, r = (seg & 3) * 32 + lane, j = j0 + c, i = i0 + r;
+        h[k] = (i < d && j < d && (!diag || j < i)) ? H[(size_t)j * d + i] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int seg = base_seg + k * kEpiWarps, c = seg >> 2, r = (seg & 3) * 32 + lane, j = j0 + c, i = i0 + r;
+        if (i < d && j < d && (!diag || j < i)) H[(size_t)j * d + i] = h[k] + tile_s[r * pitch + hh * 128 + c];
+      }
     }
-  }
-#pragma unroll
-  for (int e = 0; e < 32; e++) {
-    const int j = j0 + e;
-    if (j < d && (!diag || j < i)) H[(size_t)j * d + i] += v[e];
   }
 }
 
@@ -221,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // barriers: full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
-  volatile int* misc = reinterpret_cast<volatile int*>(bars + 2 * kStages + 5);  // [0] tmem, [1] abort, [2] last
+  volatile int* misc = reinterpret_cast<volatile int*>(bars + 2 * kStages + 5);  // [0] tmem, [1] abort
   const uint32_t ring_s = smem_u32(base);
   const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kStages;
   const uint32_t accf0 = full0 + 16 * kStages, acce0 = accf0 + 16, done_bar = acce0 + 16;
@@ -249,7 +270,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(done_bar, 1);
     misc[1] = 0;
-    misc[2] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_hi)) : "memory");
     if (prm.phases > 1) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_lo)) : "memory");
@@ -266,6 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = (uint32_t)misc[0];
   volatile int* abort = &misc[1];
+  float m_out[4][32];   // epilogue warps: this thread's row of its sub-block, round-to-nearest sums
+#pragma unroll
+  for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+    for (int e = 0; e < 32; e++) m_out[cc][e] = 0.0f;
 
   if (warp == 0) {
     // ---- TMA producer
@@ -347,15 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (tile rows) and the 128
     // columns of sub-block hh; each chunk is drained into round-to-nearest f32 registers
-    const int ew = warp - 2, q = warp & 3, hh = ew >> 2;
-    const int r = 32 * q + lane, i = ti * kBM + r, tj = 2 * tp + hh;
+    const int ew = warp - 2, q = warp & 3, hh = ew >> 2, tj = 2 * tp + hh;
     const bool live = tj <= ti && tj < prm.nt;
     const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + hh * 128;
-    float m[4][32];
-#pragma unroll
-    for (int cc = 0; cc < 4; cc++)
-#pragma unroll
-      for (int e = 0; e < 32; e++) m[cc][e] = 0.0f;
+    float(&m)[4][32] = m_out;
     bool ok = true;
     for (int c = 0; c < nchunks; c++) {
       const int b = c & 1;
@@ -382,65 +402,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort = 1;
       atomicOr(prm.status, 1);
     }
-    if (epi_all(ok && !*abort)) {
-      if (prm.splits == 1) {
-        if (live) {
-#pragma unroll
-          for (int cc = 0; cc < 4; cc++) apply32(prm.H, prm.d, i, tj * kBM + cc * 32, tj == ti, m[cc]);
-        }
-      } else {
-        float* mine = prm.partial + ((size_t)split * prm.tiles + tile) * kPartialFloats;
-        if (live) {
-#pragma unroll
-          for (int cc = 0; cc < 4; cc++) {
-            float4* dst = reinterpret_cast<float4*>(mine + ((size_t)(hh * 4 + cc) * kBM + r) * 32);
-#pragma unroll
-            for (int e = 0; e < 8; e++)
-              dst[e] = make_float4(m[cc][4 * e], m[cc][4 * e + 1], m[cc][4 * e + 2], m[cc][4 * e + 3]);
-          }
-        }
-        __threadfence();
-        epi_sync();
-        if (threadIdx.x == 64) misc[2] = (atomicAdd(&prm.counters[tile], 1) == prm.splits - 1);
-        epi_sync();
-        if (misc[2] && live) {
-          __threadfence();
-#pragma unroll 1
-          for (int cc = 0; cc < 4; cc++) {
-            float v[32];
-            const size_t off = ((size_t)(hh * 4 + cc) * kBM + r) * 32;
-#pragma unroll 1
-            for (int s = 0; s < prm.splits; s++) {
-              const float4* src =
-                  reinterpret_cast<const float4*>(prm.partial + ((size_t)s * prm.tiles + tile) * kPartialFloats + off);
-#pragma unroll
-              for (int e = 0; e < 8; e++) {
-                const float4 w = __ldcg(src + e);
-                if (s == 0) {
-                  v[4 * e] = w.x;
-                  v[4 * e + 1] = w.y;
-                  v[4 * e + 2] = w.z;
-                  v[4 * e + 3] = w.w;
-                } else {
-                  v[4 * e] += w.x;
-                  v[4 * e + 1] += w.y;
-                  v[4 * e + 2] += w.z;
-                  v[4 * e + 3] += w.w;
-                }
-              }
-            }
-            apply32(prm.H, prm.d, i, tj * kBM + cc * 32, tj == ti, v);
-          }
-        }
-      }
-    }
   }
+  // The producer has drained its loads and every MMA has completed: the ring is free and
+  // the TMEM accumulators can go.
   __syncwarp();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
+  if (warp < 2) return;
+  // ---- write-out through shared memory: tile[r][c], row pitch kBN + 1 floats
+  float* tile_s = reinterpret_cast<float*>(base);
+  const int et = threadIdx.x - 64, ew = et / 32;
+  const bool go = epi_all(!*abort);
+  if (!go) return;
+  {
+    const int q = warp & 3, hh = ew >> 2, r = 32 * q + lane;
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+      for (int e = 0; e < 32; e++) tile_s[r * (kBN + 1) + hh * 128 + cc * 32 + e] = m_out[cc][e];
+  }
+  epi_sync();
+  if (prm.splits > 1) {
+    // partial (split, tile) as row-major [128][256]: one warp per row
+    float* dst = prm.partial + ((size_t)split * prm.tiles + tile) * kPartialFloats;
+    for (int r = ew; r < kBM; r += kEpiWarps)
+#pragma unroll
+      for (int c = lane; c < kBN; c += 32) dst[r * kBN + c] = tile_s[r * (kBN + 1) + c];
+    return;
+  }
+  add_tile_to_h(prm.H, prm.d, ti, tp, prm.nt, tile_s, kBN + 1, ew, lane);
+}
+
+// Token-split reduction: one CTA per tile sums the partials of splits 0 .. S-1 in that
+// order (row-major [128][256] each) into shared memory, then adds the tile to H like the
+// direct epilogue.
+__global__ void __launch_bounds__(32 * kEpiWarps) xtx_reduce_kernel(const float* __restrict__ partial, int splits,
+                                                                   int tiles, float* __restrict__ H, int d, int nt) {
+  extern __shared__ uint8_t smem_raw[];
+  float* tile_s = reinterpret_cast<float*>(smem_raw);
+  const int tile = blockIdx.x;
+  int ti, tp;
+  tile_coords(tile, ti, tp);
+  const int t = threadIdx.x, nthr = 32 * kEpiWarps;
+  // 128 x 256 floats = 8192 float4; thread t handles float4 t + nthr * k
+  constexpr int kPer = kPartialFloats / 4 / (32 * kEpiWarps);
+#pragma unroll 1
+  for (int k0 = 0; k0 < kPer; k0 += 8) {
+    float4 acc[8];
+#pragma unroll 1
+    for (int s = 0; s < splits; s++) {
+      const float4* src = reinterpret_cast<const float4*>(partial + ((size_t)s * tiles + tile) * kPartialFloats);
+      float4 w[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) w[k] = __ldcg(src + t + nthr * (k0 + k));
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        if (s == 0) {
+          acc[k] = w[k];
+        } else {
+          acc[k].x += w[k].x;
+          acc[k].y += w[k].y;
+          acc[k].z += w[k].z;
+          acc[k].w += w[k].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int f = t + nthr * (k0 + k), r = f / (kBN / 4), c = 4 * (f % (kBN / 4));
+      float* row = tile_s + r * (kBN + 1) + c;
+      row[0] = acc[k].x;
+      row[1] = acc[k].y;
+      row[2] = acc[k].z;
+      row[3] = acc[k].w;
+    }
+  }
+  __syncthreads();
+  add_tile_to_h(H, d, ti, tp, nt, tile_s, kBN + 1, t / 32, t % 32);
 }
 
 // float32 activations -> hi = bf16(x), lo = bf16(x - hi), four elements per thread.
@@ -494,8 +535,8 @@ XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms) {
   p.ki = (int)((T + kBK - 1) / kBK);
   const int total = p.phases * p.ki;
   // cost model (microseconds): waves x steps per split at ~0.42 us per 64-token step of a
-  // 128 x 256 tile, plus the partial tiles' HBM traffic (written and read once, ~6 TB/s) and
-  // the last CTA's serial S-way read (~0.9 us per 128 KB partial)
+  // 128 x 256 tile, plus, with splits, the partial tiles' traffic (written and read once,
+  // ~6 TB/s) and the reduction launch
   int best_s = 1;
   double best = 1e300;
   const int smax = total < 2 ? 1 : (total / 2 < 32 ? total / 2 : 32);
@@ -505,7 +546,7 @@ XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms) {
     if (s_eff != s) continue;
     const double waves = (double)((p.tiles * (int64_t)s + num_sms - 1) / num_sms);
     double cost = waves * per * 0.42;
-    if (s > 1) cost += (double)p.tiles * s * 2.0 * kPartialFloats * 4 / 6e6 + 0.9 * (s + 1);
+    if (s > 1) cost += (double)p.tiles * s * 2.0 * kPartialFloats * 4 / 6e6 + 4.0;
     if (cost < best - 1e-9) {
       best = cost;
       best_s = s;
@@ -513,9 +554,8 @@ XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms) {
   }
   p.splits = best_s;
   p.steps_per_split = (total + best_s - 1) / best_s;
-  // workspace: [status 256 B][counters, 256-B padded][partials][hi][lo]
-  p.off_counters = 256;
-  p.off_partial = p.off_counters + (((size_t)p.tiles * 4 + 255) / 256) * 256;
+  // workspace: [status 256 B][partials][hi][lo]
+  p.off_partial = 256;
   p.off_hi = p.off_partial + (p.splits > 1 ? (size_t)p.splits * p.tiles * kPartialFloats * 4 : 0);
   const size_t half = f32_input ? (((size_t)T * d * 2 + 255) / 256) * 256 : 0;
   p.off_lo = p.off_hi + half;
@@ -528,7 +568,9 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(xtx_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(xtx_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kReduceSmem) !=
+            cudaSuccess)
       return 1;
     attr_set = true;
   }
@@ -547,7 +589,6 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   CUtensorMap mh, ml;
   if (int rc = make_map(&mh, hi, T, d)) return rc;
   if (int rc = make_map(&ml, lo, T, d)) return rc;
-  if (cudaMemsetAsync(w + p.off_counters, 0, (size_t)p.tiles * 4, stream) != cudaSuccess) return 1;
   XtxParams prm;
   prm.H = H;
   prm.d = (int)d;
@@ -558,10 +599,14 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   prm.ki = p.ki;
   prm.steps_per_split = p.steps_per_split;
   prm.partial = reinterpret_cast<float*>(w + p.off_partial);
-  prm.counters = reinterpret_cast<int*>(w + p.off_counters);
   prm.status = reinterpret_cast<int*>(w);
   xtx_tc_kernel<<<p.tiles * p.splits, kThreads, kSmemBytes, stream>>>(mh, ml, prm);
   note_launch();
+  if (p.splits > 1) {
+    xtx_reduce_kernel<<<p.tiles, 32 * kEpiWarps, kReduceSmem, stream>>>(
+        reinterpret_cast<const float*>(w + p.off_partial), p.splits, p.tiles, H, (int)d, p.nt);
+    note_launch();
+  }
   return 0;
 }
 

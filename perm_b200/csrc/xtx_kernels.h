@@ -14,7 +14,7 @@ struct XtxPlan {
   int ki;               // 64-token steps per phase
   int splits;           // token splits
   int steps_per_split;
-  size_t off_counters, off_partial, off_hi, off_lo, ws_bytes;
+  size_t off_partial, off_hi, off_lo, ws_bytes;
 };
 
 XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms);
