@@ -26,8 +26,8 @@
 //
 // Token splits.  When there are too few tiles to fill the SMs, tokens are cut into S splits
 // of whole 64-token steps.  Each split CTA writes its f32 partial tile to the workspace; a
-// second kernel sums the S partials of each tile in split order 0..S-1 and adds the sum to H
-// the same way.  Repeated runs give identical bits and no CTA waits for another.
+// second kernel (eight CTAs per tile) sums the S partials in split order 0..S-1 and adds the
+// sum to H the same way.  Repeated runs give identical bits and no CTA waits for another.
 //
 // float32 activations.  The reference casts activations to float32 before the product and
 // small teachers run in float32.  For those inputs X is first split into two bf16 arrays,
@@ -65,7 +65,6 @@ constexpr uint32_t kTmemCols = 2 * kBN;              // two accumulators (double
 constexpr int kPartialFloats = kBM * kBN;            // 128 KB per (tile, split) partial
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
-constexpr int kReduceSmem = kBM * (kBN + 1) * 4;   // staged tile, 131.6 KB
 
 // UMMA instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12
 // = 1), both MN-major (bits 15, 16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -436,52 +435,81 @@ __global__ void __launch_bounds__(kThreads, 1)
   add_tile_to_h(prm.H, prm.d, ti, tp, prm.nt, tile_s, kBN + 1, ew, lane);
 }
 
-// Token-split reduction: one CTA per tile sums the partials of splits 0 .. S-1 in that
-// order (row-major [128][256] each) into shared memory, then adds the tile to H like the
-// direct epilogue.
-__global__ void __launch_bounds__(32 * kEpiWarps) xtx_reduce_kernel(const float* __restrict__ partial, int splits,
-                                                                   int tiles, float* __restrict__ H, int d, int nt) {
-  extern __shared__ uint8_t smem_raw[];
-  float* tile_s = reinterpret_cast<float*>(smem_raw);
-  const int tile = blockIdx.x;
+// Token-split reduction.  One CTA per (tile, sub-block hh, 32-row group): it sums that
+// 32 x 128 slice of the partials of splits 0 .. S-1 in that order (partials are row-major
+// [128][256]), stages the sum in shared memory and adds it to H[i, j] and to the mirror
+// H[j, i] with 128-byte row segments, loads batched ahead of stores.
+__global__ void __launch_bounds__(256) xtx_reduce_kernel(const float* __restrict__ partial, int splits, int tiles,
+                                                         float* __restrict__ H, int d, int nt) {
+  __shared__ float sv[32][129];
+  const int tile = blockIdx.x >> 3, hh = (blockIdx.x >> 2) & 1, rg = blockIdx.x & 3;
   int ti, tp;
   tile_coords(tile, ti, tp);
-  const int t = threadIdx.x, nthr = 32 * kEpiWarps;
-  // 128 x 256 floats = 8192 float4; thread t handles float4 t + nthr * k
-  constexpr int kPer = kPartialFloats / 4 / (32 * kEpiWarps);
+  const int tj = 2 * tp + hh;
+  if (tj > ti || tj >= nt) return;
+  const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+  const int i0 = ti * kBM + rg * 32, j0 = tj * kBM;
+  const bool diag = tj == ti;
+  // slice = 32 rows x 32 float4; thread t takes float4 t + 256 k: row (t + 256 k) / 32, column lane
+  float4 acc[4];
 #pragma unroll 1
-  for (int k0 = 0; k0 < kPer; k0 += 8) {
-    float4 acc[8];
-#pragma unroll 1
-    for (int s = 0; s < splits; s++) {
-      const float4* src = reinterpret_cast<const float4*>(partial + ((size_t)s * tiles + tile) * kPartialFloats);
-      float4 w[8];
+  for (int s = 0; s < splits; s++) {
+    const float4* src = reinterpret_cast<const float4*>(partial + ((size_t)s * tiles + tile) * kPartialFloats +
+                                                        (size_t)(rg * 32) * kBN + hh * 128);
+    float4 w[4];
 #pragma unroll
-      for (int k = 0; k < 8; k++) w[k] = __ldcg(src + t + nthr * (k0 + k));
+    for (int k = 0; k < 4; k++) w[k] = __ldcg(src + (size_t)(warp + 8 * k) * (kBN / 4) + lane);
 #pragma unroll
-      for (int k = 0; k < 8; k++) {
-        if (s == 0) {
-          acc[k] = w[k];
-        } else {
-          acc[k].x += w[k].x;
-          acc[k].y += w[k].y;
-          acc[k].z += w[k].z;
-          acc[k].w += w[k].w;
-        }
+    for (int k = 0; k < 4; k++) {
+      if (s == 0) {
+        acc[k] = w[k];
+      } else {
+        acc[k].x += w[k].x;
+        acc[k].y += w[k].y;
+        acc[k].z += w[k].z;
+        acc[k].w += w[k].w;
       }
     }
+  }
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      const int f = t + nthr * (k0 + k), r = f / (kBN / 4), c = 4 * (f % (kBN / 4));
-      float* row = tile_s + r * (kBN + 1) + c;
-      row[0] = acc[k].x;
-      row[1] = acc[k].y;
-      row[2] = acc[k].z;
-      row[3] = acc[k].w;
-    }
+  for (int k = 0; k < 4; k++) {
+    float* row = &sv[warp + 8 * k][4 * lane];
+    row[0] = acc[k].x;
+    row[1] = acc[k].y;
+    row[2] = acc[k].z;
+    row[3] = acc[k].w;
   }
   __syncthreads();
-  add_tile_to_h(H, d, ti, tp, nt, tile_s, kBN + 1, t / 32, t % 32);
+  // direct: 32 rows x 4 column chunks; warp w takes segments w, w + 8, ... (16 each)
+  {
+    float h[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int seg = warp + 8 * k, r = seg >> 2, i = i0 + r, j = j0 + (seg & 3) * 32 + lane;
+      h[k] = (i < d && j < d && (!diag || j <= i)) ? H[(size_t)i * d + j] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int seg = warp + 8 * k, r = seg >> 2, c = (seg & 3) * 32 + lane, i = i0 + r, j = j0 + c;
+      if (i < d && j < d && (!diag || j <= i)) H[(size_t)i * d + j] = h[k] + sv[r][c];
+    }
+  }
+  // mirror: 128 columns j, lanes over the 32 rows i; warp w takes columns w, w + 8, ...
+  {
+    const int i = i0 + lane;
+    float h[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int j = j0 + warp + 8 * k;
+      h[k] = (i < d && j < d && (!diag || j < i)) ? H[(size_t)j * d + i] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int c = warp + 8 * k, j = j0 + c;
+      if (i < d && j < d && (!diag || j < i)) H[(size_t)j * d + i] = h[k] + sv[lane][c];
+    }
+  }
+  (void)tiles;
 }
 
 // float32 activations -> hi = bf16(x), lo = bf16(x - hi), four elements per thread.
@@ -568,9 +596,7 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(xtx_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(xtx_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kReduceSmem) !=
-            cudaSuccess)
+        cudaSuccess)
       return 1;
     attr_set = true;
   }
@@ -603,8 +629,8 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   xtx_tc_kernel<<<p.tiles * p.splits, kThreads, kSmemBytes, stream>>>(mh, ml, prm);
   note_launch();
   if (p.splits > 1) {
-    xtx_reduce_kernel<<<p.tiles, 32 * kEpiWarps, kReduceSmem, stream>>>(
-        reinterpret_cast<const float*>(w + p.off_partial), p.splits, p.tiles, H, (int)d, p.nt);
+    xtx_reduce_kernel<<<p.tiles * 8, 256, 0, stream>>>(reinterpret_cast<const float*>(w + p.off_partial), p.splits,
+                                                       p.tiles, H, (int)d, p.nt);
     note_launch();
   }
   return 0;
