@@ -101,8 +101,9 @@ int cp_factor_u(const double* H, int64_t n, const int32_t* order, double diag_sh
 int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double diag_shift, double* U_out,
                     void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
 
-/* Device layout of U for the sweep: a column-pair-interleaved transpose plus the diagonal,
- * cp_ef_u_bytes(n) bytes.  Built once per factor (q/k/v and gate/up share theirs). */
+/* Device layout of U for the sweep: U row-major float32 [n][n] followed by its diagonal,
+ * cp_ef_u_bytes(n) bytes (U and u_prepared 16-byte aligned).  Built once per factor (q/k/v
+ * and gate/up share theirs). */
 size_t cp_ef_u_bytes(int64_t n);
 int cp_ef_prepare_u(const float* U, int64_t n, float* u_prepared, void* stream);
 
@@ -130,9 +131,9 @@ int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const in
  * reference: it exists for hosts whose device memory is owned by another allocator (a
  * framework's caching allocator, a serving runtime that reserves the whole GPU up front) or
  * that reach this library through an FFI with no way to allocate or pass a scratch buffer.
- * The sweep's working rows go to a fixed array of CP_NOALLOC_SCRATCH_BYTES inside the
+ * The sweep's per-row errors go to a fixed array of CP_NOALLOC_SCRATCH_BYTES inside the
  * library, held on every GPU that loads it until the process exits; this call itself
- * allocates nothing.  Shapes with ceil(nrow/32)*32 * n * 4 > CP_NOALLOC_SCRATCH_BYTES are
+ * allocates nothing.  Shapes with ceil(nrow/128)*128 * n * 4 > CP_NOALLOC_SCRATCH_BYTES are
  * rejected with CP_ERR_WORKSPACE.  The first call on a device looks the array's address up
  * (make that call before any stream capture).  All calls share the array: calls that
  * overlap on the GPU (other streams, other threads) race and must be serialised. */

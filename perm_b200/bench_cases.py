@@ -3,8 +3,10 @@
 on the device and runs its kernels a few times.
 
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
+    sweep_layers  eight Qwen3-0.6B-shaped layers (56 tensors), grouped EF sweep
     fit      Q2_K imatrix fit of a 4096 x 4096 tensor
     factor   batched FP64 factorisation of 16 Hessians n = 1024 and 4 of n = 3072
+    factor_model  the whole 0.6B model's 112 factorisations
     xtx      X^T X of 32768 bf16 tokens at d = 1024, 2048, 3072 (tcgen05 kernel)
     xtx_f32  the same with float32 tokens (hi/lo bf16 split, four products)
 """
@@ -22,17 +24,15 @@ def _hess(torch, n, seed, T=4096):
     return X.T @ X / T
 
 
-def case_sweep(torch, reps):
+def _sweep_case(torch, reps, shapes):
     from . import _native as nat
     from .encoder import Encoder, Job
-    shapes = [(1024, 1024, "Q2_K")] * 24 + [(1024, 3072, "Q3_K")] * 8
     hs, jobs = {}, []
-    for i, (nrow, n, tt) in enumerate(shapes):
-        k = f"h{n}"
-        if k not in hs:
-            hs[k] = _hess(torch, n, n)
+    for i, (nrow, n, tt, hk) in enumerate(shapes):
+        if hk not in hs:
+            hs[hk] = _hess(torch, n, len(hs) + n)
         x = torch.randn(nrow, n, device="cuda") * 0.02
-        jobs.append(Job(f"t{i}", tt, "EF", x, torch.diagonal(hs[k]).float().contiguous(), k))
+        jobs.append(Job(f"t{i}", tt, "EF", x, torch.diagonal(hs[hk]).float().contiguous(), hk))
     enc = Encoder()
     f = enc.factor(hs)
     enc.encode(jobs, f, stats=False)
@@ -43,9 +43,30 @@ def case_sweep(torch, reps):
     torch.cuda.synchronize()
     nat.profile_enable(False)
     p = nat.profile_collect()
-    upd = sum(2 * r * n * (n - 1) / 2 for r, n, _ in shapes)
+    upd = sum(2 * r * n * (n - 1) / 2 for r, n, _, _ in shapes)
     ms = p["sweep"][0] / reps
+    return ms, upd
+
+
+def case_sweep(torch, reps):
+    """24 Q2_K tensors 1024 x 1024 + 8 Q3_K tensors 1024 x 3072 (256 CTAs: under one wave)."""
+    shapes = [(1024, 1024, "Q2_K", "h1024")] * 24 + [(1024, 3072, "Q3_K", "h3072")] * 8
+    ms, upd = _sweep_case(torch, reps, shapes)
     return f"sweep: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s"
+
+
+def case_sweep_layers(torch, reps):
+    """Eight Qwen3-0.6B-shaped layers (q, k, v, o, gate, up, down; Q2_K/Q3_K mixture shapes),
+    each layer with its own four Hessians: 768 CTAs, the whole-model sweep's mix of n."""
+    shapes = []
+    for l in range(8):
+        shapes += [(2048, 1024, "Q2_K", f"qkv{l}"), (1024, 1024, "Q2_K", f"qkv{l}"), (1024, 1024, "Q2_K", f"qkv{l}"),
+                   (1024, 2048, "Q2_K", f"o{l}"), (3072, 1024, "Q2_K", f"gu{l}"), (3072, 1024, "Q2_K", f"gu{l}"),
+                   (1024, 3072, "Q3_K", f"d{l}")]
+    shapes.sort(key=lambda s: -s[1])
+    ms, upd = _sweep_case(torch, reps, shapes)
+    return (f"sweep_layers: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s, "
+            f"{2 * upd / ms / 1e9:.2f} T fp32 lane-ops/s")
 
 
 def case_fit(torch, reps):
@@ -88,6 +109,28 @@ def _xtx_tile_flops(T, d):
     return 2.0 * tiles * 128 * 256 * T
 
 
+def case_factor_model(torch, reps):
+    """The whole Qwen3-0.6B-shaped model's 112 factorisations (56 at n = 1024, 28 at 2048,
+    28 at 3072) through Encoder.factor, wall time with a device sync."""
+    from .encoder import Encoder
+    base = {1024: _hess(torch, 1024, 1), 2048: _hess(torch, 2048, 2), 3072: _hess(torch, 3072, 3)}
+    hs = {}
+    for l in range(28):
+        for k, n in (("qkv", 1024), ("o", 2048), ("gu", 1024), ("d", 3072)):
+            hs[f"{k}{l}"] = base[n] * (1.0 + 0.01 * l)
+    ds = {k: torch.diagonal(v).cpu().numpy() for k, v in hs.items()}
+    enc = Encoder()
+    enc.factor(hs, ds)
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        enc.factor(hs, ds)
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t) / reps
+    fl = (2.0 / 3.0) * 28 * (2 * 1024 ** 3 + 2048 ** 3 + 3072 ** 3)
+    return f"factor_model 112 Hessians: {dt * 1e3:.2f} ms, {fl / dt / 1e12:.2f} FP64 TFLOP/s"
+
+
 def case_xtx(torch, reps, dtype="bf16"):
     from . import hessians
     out = []
@@ -118,7 +161,7 @@ def case_xtx_f32(torch, reps):
     return case_xtx(torch, reps, "f32")
 
 
-CASES = {"sweep": case_sweep, "fit": case_fit, "factor": case_factor, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
+CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):

@@ -214,12 +214,13 @@ int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double dia
   return factor_common(H, n, order, diag_shift, U_out, true, workspace, ws_bytes, status_dev, stream);
 }
 
-size_t cp_ef_u_bytes(int64_t n) { return n > 0 ? cpk::ef_ut2_bytes(n) : 0; }
+size_t cp_ef_u_bytes(int64_t n) { return n > 0 ? cpk::ef_u_prepared_bytes(n) : 0; }
 
-int cp_ef_prepare_u(const float* U, int64_t n, float* ut2_and_diag, void* stream) {
+int cp_ef_prepare_u(const float* U, int64_t n, float* u_prepared, void* stream) {
   if (n <= 0 || n % 256) return set_err(CP_ERR_SHAPE, "n must be a positive multiple of 256");
-  if (!U || !ut2_and_diag) return set_err(CP_ERR_ARG, "null pointer");
-  return check_rc(cpk::launch_build_ut2(U, n, ut2_and_diag, ut2_and_diag + (size_t)n * n, (cudaStream_t)stream),
+  if (!U || !u_prepared) return set_err(CP_ERR_ARG, "null pointer");
+  if ((((uintptr_t)U) | ((uintptr_t)u_prepared)) & 15) return set_err(CP_ERR_ARG, "U and u_prepared must be 16-byte aligned");
+  return check_rc(cpk::launch_prepare_u(U, n, u_prepared, (cudaStream_t)stream),
                   "cp_ef_prepare_u");
 }
 
@@ -238,7 +239,7 @@ int cp_ef_sweep(int t, const float* x, int64_t nrow, int64_t n, const int32_t* o
   if (!x || !order || !ut2 || !dl || (hm && !ml) || !codes || !workspace) return set_err(CP_ERR_ARG, "null pointer");
   if (ws_bytes < cpk::ef_sweep_workspace_bytes(nrow, n)) return set_err(CP_ERR_WORKSPACE, "sweep workspace too small");
   ProfScope ps(kProfSweep, (cudaStream_t)stream);
-  return check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, ut2 + (size_t)n * n, dl, ml, workspace, codes,
+  return check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, dl, ml, workspace, codes,
                                        w_out, (cudaStream_t)stream),
                   "cp_ef_sweep");
 }
@@ -301,7 +302,7 @@ int cp_ef_encode(int t, const float* x, int64_t nrow, int64_t n, const int32_t* 
     if ((rc = check_rc(cpk::launch_grid_params(t, out, nrow, n, dl, ml, s), "cp_ef_encode: grid"))) return rc;
     {
       ProfScope ps(kProfSweep, s);
-      if ((rc = check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, ut2 + (size_t)n * n, dl, ml, ws + L.sweep,
+      if ((rc = check_rc(cpk::launch_ef_sweep(t, x, nrow, n, order, ut2, dl, ml, ws + L.sweep,
                                               codes, it + 1 < n_iter ? wcur : nullptr, s),
                          "cp_ef_encode: sweep")))
         return rc;
@@ -402,10 +403,6 @@ int cp_weighted_err_batch(const cp_block_job* jobs, int count, void* stream) {
 int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
   cudaStream_t s = (cudaStream_t)stream;
-  int64_t all_tiles = 0;
-  for (int i = 0; i < count; i++) all_tiles += (jobs[i].nrow + 31) / 32;
-  // one-warp CTAs only when there are enough tiles to keep ~16 resident per SM
-  const int warps = all_tiles >= 2 * 16 * 148 ? 1 : 8;
   static thread_local cpk::SweepBatch b;
   b.count = 0;
   int tiles = 0;
@@ -413,7 +410,7 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
     const bool flush = (i == count) || b.count == cpk::kSweepBatchMax;
     if (flush && b.count) {
       ProfScope ps(kProfSweep, s);
-      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, warps, s), "cp_ef_sweep_batch")) return rc;
+      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, s), "cp_ef_sweep_batch")) return rc;
       b.count = 0;
       tiles = 0;
     }
@@ -430,7 +427,7 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
     if (d.ml == nullptr && (j.ggml_type == cpk::kQ2_K || j.ggml_type == cpk::kQ4_K || j.ggml_type == cpk::kQ5_K))
       return set_err(CP_ERR_ARG, "ml is required for Q2_K/Q4_K/Q5_K");
     d.tile0 = tiles;
-    tiles += (int)((j.nrow + 31) / 32);
+    tiles += cpk::sweep_ctas(j.nrow);
     b.count++;
   }
   return CP_OK;

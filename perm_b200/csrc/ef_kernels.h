@@ -5,14 +5,16 @@
 #include <cuda_runtime.h>
 
 namespace cpk {
-// One tensor of a grouped error-feedback sweep launch (tiles [tile0, tile0 + ceil(nrow/32))).
+// Rows per sweep CTA = 32 * kSweepWarps.
+constexpr int kSweepWarps = 4;
+// One tensor of a grouped error-feedback sweep launch (CTAs [tile0, tile0 + sweep_ctas(nrow))).
 struct SweepDesc {
   const float* x;
   const int* order;
-  const float* ut2;   // prepared U: interleaved transpose, then the diagonal
+  const float* u;     // prepared U: row-major float32 [n][n], then the diagonal
   const float* dl;
   const float* ml;    // null for types without a min
-  float2* work;
+  float* work;        // errors, [32-row tile][n][32]
   int8_t* codes;
   float* wout;        // null in the last round
   int nrow, n, sbw, lo, hi, tile0;
@@ -22,19 +24,19 @@ struct SweepBatch {
   int count;
   SweepDesc d[kSweepBatchMax];
 };
-bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* ut2,
+bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
                 const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d);
-int launch_ef_sweep_batch(const SweepBatch& b, int total_tiles, int warps, cudaStream_t stream);
+int sweep_ctas(int64_t nrow);
+int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream);
 // Sweep with its working rows in a fixed per-device array (no caller workspace).
 constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
-int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* UT2,
+int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
                             const float* dl, const float* ml, int8_t* codes, float* wcur, cudaStream_t stream);
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n);
-size_t ef_ut2_bytes(int64_t n);
-int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream);
-int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order,
-                    const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
-                    int8_t* codes, float* wcur, cudaStream_t stream);
+size_t ef_u_prepared_bytes(int64_t n);
+int launch_prepare_u(const float* U, int64_t n, float* out, cudaStream_t stream);
+int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
+                    const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, cudaStream_t stream);
 size_t factor_workspace_bytes(int64_t n);
 // Same-size factorisations advanced step by step together (grid y / z index the item).
 constexpr int kFactorBatchMax = 64;

@@ -4,18 +4,22 @@
 //   q  = clip(nearest_int((w[jj] + ml) / dl), lo, hi)     (q = 0, e = 0 where dl == 0)
 //   e  = (w[jj] - (dl*q - ml)) / U[jj][jj]
 //   w[k] = fl(w[k] - fl(e * U[jj][k]))   for every k > jj, in ascending jj order
-// Rows are independent, so a CTA owns a tile of 32 rows and runs the whole sweep for them
-// with no inter-CTA synchronisation.  Columns are processed in blocks of 32:
-//   panel    (warp 0, lane = row): the 32 sequential quantize/error steps of the block with
-//            its in-block updates, in registers;
-//   trailing (8 warps): every later column gets the block's 32 updates in jj order, two
-//            columns at a time with packed f32x2 arithmetic that rounds the product and the
-//            difference separately (see upd2), so each element sees exactly the
-//            reference's rounding sequence.
-// The working rows live in a global workspace laid out [tile][column pair][32 rows][2]
-// (coalesced float2 per lane); U is read from a column-pair-interleaved transpose
-// UT2[pair][jj][2] so one 16-byte broadcast load feeds two jj steps of a column pair.
+// Rows are independent.  A CTA of kSweepWarps = 4 warps owns 128 rows (lane = row) and walks the
+// columns in act order in blocks of 64, left-looking:
+//   1. the row's 64 working values of the block are gathered from x into registers;
+//   2. the errors of every earlier column are applied in ascending jj: per jj, each thread
+//      updates its 64 values with e_jj * U[jj][block] (32 independent packed pairs, see
+//      upd2), U rows and the stored errors streamed through a shared-memory cp.async ring
+//      that the four warps share;
+//   3. the block's panel: the 64 dependent quantize/error steps, each followed by its
+//      in-block updates, in registers (four sub-panels of 16 in a run-time loop); the
+//      errors go to the workspace for later blocks.
+// Every element therefore receives exactly the reference's updates, in the reference's
+// order, each rounded as the reference rounds it.  Per row, the workspace holds the n
+// errors (written once, read once per later block), instead of a working copy of the row
+// that a right-looking sweep would rewrite after every block.
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <mutex>
 #include "kq_common.cuh"
 #include "kquant_kernels.h"
@@ -40,24 +44,15 @@ __device__ __forceinline__ void upd2(float& wx, float& wy, float ex, float ey, f
       : "f"(ex), "f"(ey), "f"(ux), "f"(uy), "f"(nz));
 }
 
-// UT2[kp][jj][p] = U[jj][2kp+p] for jj <= 2kp+p, else 0; diagU[jj] = U[jj][jj].
-__global__ void build_ut2_kernel(const float* __restrict__ U, int n, float* __restrict__ UT2,
-                                 float* __restrict__ diagU) {
-  __shared__ float t[32][33];
-  const int k0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 256 threads: ty 0..7
-  for (int r = ty; r < 32; r += 8) {
-    const int jj = j0 + r, k = k0 + tx;
-    t[r][tx] = (jj <= k) ? U[(size_t)jj * n + k] : 0.0f;
-    if (jj == k) diagU[jj] = U[(size_t)jj * n + k];
-  }
-  __syncthreads();
-  // output: for column pair kp = (k0/2) + c (c 0..15), jj = j0 + r: 64 floats per kp row segment
-  for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-    const int c = i >> 6, rem = i & 63, r = rem >> 1, p = rem & 1;
-    const int kp = (k0 >> 1) + c;
-    UT2[((size_t)kp * n + j0 + r) * 2 + p] = t[r][2 * c + p];
-  }
+// Prepared U for the sweep: U row-major (float32 [n][n]) followed by its diagonal.
+__global__ void prepare_u_kernel(const float* __restrict__ U, int n, float* __restrict__ out) {
+  const size_t n4 = (size_t)n * n / 4;
+  const float4* src = reinterpret_cast<const float4*>(U);
+  float4* dst = reinterpret_cast<float4*>(out);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[(size_t)n * n + i] = U[(size_t)i * n + i];
 }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -68,136 +63,172 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Sweep of one 32-row tile of one tensor.  WARPS warps per CTA: warp 0 runs the panels,
-// all WARPS warps share the trailing updates (WARPS = 1: one warp does everything and keeps
-// the block's errors in registers, many such CTAs per SM hide each other's panel latency;
-// WARPS = 8: for launches with few tiles).  Each warp streams the column pairs it updates
-// (the U segment and the 32 working rows, 512 bytes a pair) through a 4-stage cp.async ring
-// in shared memory, so global latency overlaps the update chains.
-template <int WARPS>
-__device__ __forceinline__ void sweep_tile(const SweepDesc& t, int tile, float nz) {
-  constexpr int ST = 4;
-  __shared__ float s_u[32][33];
-  __shared__ __align__(16) float2 s_e[WARPS == 1 ? 1 : 32][32];
-  __shared__ int s_ord[32];
-  __shared__ __align__(16) float4 s_ring[WARPS][ST][32];
-  constexpr int NT = 32 * WARPS;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+constexpr int kSwB = 64;      // columns per block
+constexpr int kSwJS = 8;      // earlier columns (jj) per ring stage
+constexpr int kSwST = 4;      // ring stages
+constexpr int kSwThreads = 32 * kSweepWarps;
+
+struct SweepSmem {
+  __align__(16) float ud[kSwB][kSwB];                // ud[a][b] = U[j0+a][j0+b], the block's diagonal block
+  float dg[kSwB];                                    // U[j0+a][j0+a]
+  int ord[kSwB];                                     // order[j0+a]
+  __align__(16) float ru[kSwST][kSwJS][kSwB];        // ring: U[jj][j0 .. j0+63]
+  __align__(16) float re[kSwST][kSweepWarps][kSwJS][32];  // ring: errors e_jj of each warp's rows
+};
+
+// One CTA = kSweepWarps x 32 rows of one tensor.
+__device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz) {
+  __shared__ SweepSmem sm;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = t.n, nrow = t.nrow;
-  const int row = tile * 32 + lane;
+  const int tile32 = cta * kSweepWarps + warp;
+  const int row = tile32 * 32 + lane;
   const bool rv = row < nrow;
-  const int npair = n >> 1;
-  const int sbw = t.sbw, lo = t.lo, hi = t.hi;
-  const int nsub = n / sbw;
-  const int* __restrict__ order = t.order;
-  const float* __restrict__ UT2 = t.ut2;
-  const float* __restrict__ diagU = t.ut2 + (size_t)n * n;
-  float2* W = t.work + (size_t)tile * npair * 32;
-  const float* xr = t.x + (size_t)row * n;
+  const int sbw = t.sbw, lo = t.lo, hi = t.hi, nsub = n / sbw;
+  const float* __restrict__ U = t.u;
+  const float* __restrict__ diagU = t.u + (size_t)n * n;
+  float* __restrict__ E = t.work;                              // [tile32][n][32]
+  const float* __restrict__ Ecta = t.work + (size_t)cta * kSweepWarps * n * 32;
+  float* __restrict__ Erow = E + (size_t)tile32 * n * 32 + lane;
+  const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * n;
+  const float* __restrict__ dlr = t.dl + (size_t)(rv ? row : 0) * nsub;
+  const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * nsub : nullptr;
+  int8_t* __restrict__ codes = t.codes + (size_t)row * n;
+  float* __restrict__ wout = t.wout ? t.wout + (size_t)row * n : nullptr;
 
-  // wp = x[:, order]
-  for (int kp = warp; kp < npair; kp += WARPS) {
-    float2 v = make_float2(0.0f, 0.0f);
-    if (rv) {
-      v.x = __ldg(xr + __ldg(order + 2 * kp));
-      v.y = __ldg(xr + __ldg(order + 2 * kp + 1));
+  for (int j0 = 0; j0 < n; j0 += kSwB) {
+    __syncthreads();  // the previous block's readers of the shared buffers are done
+    const int nst = j0 / kSwJS;
+    // stage s = U rows jj in [s*JS, s*JS + JS) of this block's columns + the CTA's errors
+    // of those jj (16 + 8 * kSweepWarps = 48 chunks of 16 bytes per jj)
+    auto issue = [&](int s) {
+      if (s < nst) {
+        const int st = s % kSwST, jj0 = s * kSwJS;
+        for (int c = tid; c < kSwJS * (16 + 8 * kSweepWarps); c += kSwThreads) {
+          if (c < kSwJS * 16) {
+            const int k = c >> 4, c4 = c & 15;
+            cp_async16(&sm.ru[st][k][4 * c4], U + (size_t)(jj0 + k) * n + j0 + 4 * c4);
+          } else {
+            const int c2 = c - kSwJS * 16, w = c2 / (kSwJS * 8), rem = c2 % (kSwJS * 8);
+            const int k = rem >> 3, l4 = rem & 7;
+            cp_async16(&sm.re[st][w][k][4 * l4], Ecta + ((size_t)w * n + jj0 + k) * 32 + 4 * l4);
+          }
+        }
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < kSwST - 1; s++) issue(s);
+    for (int i = tid; i < kSwB * kSwB / 4; i += kSwThreads) {
+      const int a = i >> 4, c4 = i & 15;
+      reinterpret_cast<float4*>(sm.ud[a])[c4] =
+          __ldg(reinterpret_cast<const float4*>(U + (size_t)(j0 + a) * n + j0) + c4);
     }
-    W[kp * 32 + lane] = v;
-  }
-  __syncthreads();
-
-  float2 ee[32];
-  for (int j0 = 0; j0 < n; j0 += 32) {
-    for (int i = threadIdx.x; i < 32 * 32; i += NT) {  // s_u[a][b] = U[j0+a][j0+b]
-      const int a = i & 31, b = i >> 5;
-      s_u[a][b] = __ldg(UT2 + ((size_t)((j0 + b) >> 1) * n + j0 + a) * 2 + (b & 1));
+    if (tid < kSwB) {
+      sm.ord[tid] = __ldg(t.order + j0 + tid);
+      sm.dg[tid] = __ldg(diagU + j0 + tid);
     }
-    if (threadIdx.x < 32) s_ord[threadIdx.x] = __ldg(order + j0 + threadIdx.x);
     __syncthreads();
 
-    if (warp == 0) {
-      float w[32], dlv[32], mlv[32];
+    // 1. the block's working values, w = x[row, order[j0 + c]]
+    float w[kSwB];
 #pragma unroll
-      for (int a = 0; a < 16; a++) {
-        const float2 v = W[((j0 >> 1) + a) * 32 + lane];
-        w[2 * a] = v.x;
-        w[2 * a + 1] = v.y;
+    for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c]) : 0.0f;
+
+    // 2. errors of every earlier column, ascending jj
+    for (int s = 0; s < nst; s++) {
+      cp_async_wait<kSwST - 2>();
+      __syncthreads();  // stage s landed for everyone; everyone is done with stage s - 1
+      issue(s + kSwST - 1);
+      const int st = s % kSwST;
+#pragma unroll 2
+      for (int k = 0; k < kSwJS; k++) {
+        const float e = sm.re[st][warp][k][lane];
+        const float4* u4 = reinterpret_cast<const float4*>(sm.ru[st][k]);
+#pragma unroll
+        for (int c4 = 0; c4 < kSwB / 4; c4++) {
+          const float4 u = u4[c4];
+          upd2(w[4 * c4], w[4 * c4 + 1], e, e, u.x, u.y, nz);
+          upd2(w[4 * c4 + 2], w[4 * c4 + 3], e, e, u.z, u.w, nz);
+        }
       }
-      const float* dlr = t.dl + (size_t)row * nsub;
-      const float* mlr = t.ml ? t.ml + (size_t)row * nsub : nullptr;
+    }
+    cp_async_wait<0>();
+
+    // 3. panel: the block's 64 dependent quantize/error steps, as four sub-panels of 16
+    // (a run-time loop).  Sub-panel p quantizes w[0..15] in order, each step followed by its
+    // updates of the later columns of the sub-panel; then the 16 errors update the block's
+    // remaining 16-column groups (ascending jj, packed); then w shifts down by 16 registers so
+    // the next sub-panel again finds its columns in w[0..15].  Register indices stay
+    // compile-time and no update is computed that the reference does not make.
+    // dl/ml of sub-panel p + 1 are fetched while sub-panel p runs
+    float pd[16], pm[16];
 #pragma unroll
-      for (int a = 0; a < 32; a++) {  // independent loads, issued ahead of the dependent chain
-        const int sidx = s_ord[a] / sbw;
-        dlv[a] = rv ? __ldg(dlr + sidx) : 0.0f;
-        mlv[a] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+    for (int i = 0; i < 16; i++) {
+      const int sidx = sm.ord[i] / sbw;
+      pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
+      pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+    }
+#pragma unroll 1
+    for (int p = 0; p < kSwB / 16; p++) {
+      const int a0 = 16 * p;
+      float es[16];
+      float cd[16], cm[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        cd[i] = pd[i];
+        cm[i] = pm[i];
+      }
+      if (p + 1 < kSwB / 16) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int sidx = sm.ord[a0 + 16 + i] / sbw;
+          pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
+          pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+        }
       }
 #pragma unroll
-      for (int a = 0; a < 32; a++) {
-        const int j = s_ord[a];
+      for (int i = 0; i < 16; i++) {
+        const int a = a0 + i, j = sm.ord[a];
+        const float dlv = cd[i], mlv = cm[i], wa = w[i];
         int q = 0;
         float e = 0.0f;
-        if (dlv[a] != 0.0f) {
-          q = clampi(nint((w[a] + mlv[a]) / dlv[a]), lo, hi);
-          const float recon = dlv[a] * (float)q - mlv[a];
-          e = (w[a] - recon) / __ldg(diagU + j0 + a);
+        if (dlv != 0.0f) {
+          q = clampi(nint((wa + mlv) / dlv), lo, hi);
+          const float recon = dlv * (float)q - mlv;
+          e = (wa - recon) / sm.dg[a];
         }
         if (rv) {
-          t.codes[(size_t)row * n + j] = (int8_t)q;
-          if (t.wout) t.wout[(size_t)row * n + j] = w[a];
+          codes[j] = (int8_t)q;
+          if (wout) wout[j] = wa;
         }
-        if constexpr (WARPS == 1) ee[a] = make_float2(e, e);
-        else s_e[a][lane] = make_float2(e, e);
+        Erow[(size_t)(j0 + a) * 32] = e;
+        es[i] = e;
 #pragma unroll
-        for (int b = a + 1; b < 32; b++) w[b] = w[b] - e * s_u[a][b];
+        for (int b = i + 1; b < 16; b++) w[b] = w[b] - e * sm.ud[a][a0 + b];
       }
+      // later 16-column groups g of the block (columns a0 + 16 g .. +15 are w[16 g ..])
+#pragma unroll
+      for (int g = 1; g < 4; g++) {
+        if (p + g < kSwB / 16) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[a0 + i][a0 + 16 * g]);
+#pragma unroll
+            for (int c2 = 0; c2 < 8; c2++) {
+              const float2 u = u2[c2];
+              upd2(w[16 * g + 2 * c2], w[16 * g + 2 * c2 + 1], es[i], es[i], u.x, u.y, nz);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kSwB - 16; c++) w[c] = w[c + 16];
     }
-    if constexpr (WARPS > 1) __syncthreads();
-
-    const int kp0 = (j0 + 32) >> 1;
-    const int first = kp0 + warp;
-    const int count = first < npair ? (npair - first + WARPS - 1) / WARPS : 0;
-    if (count > 0) {
-      if constexpr (WARPS > 1) {
-#pragma unroll
-        for (int a = 0; a < 32; a++) ee[a] = s_e[a][lane];
-      }
-      // lanes 0-15 fetch the pair's 64 U values, lanes 16-31 its 32 working-row float2s
-      auto issue = [&](int i) {
-        if (i < count) {
-          const int kp = first + i * WARPS;
-          const float4* src = lane < 16
-              ? reinterpret_cast<const float4*>(UT2 + ((size_t)kp * n + j0) * 2) + lane
-              : reinterpret_cast<const float4*>(W + (size_t)kp * 32) + (lane - 16);
-          cp_async16(&s_ring[warp][i % ST][lane], src);
-        }
-        cp_async_commit();
-      };
-#pragma unroll
-      for (int i = 0; i < ST - 1; i++) issue(i);
-      for (int i = 0; i < count; i++) {
-        issue(i + ST - 1);
-        cp_async_wait<ST - 1>();
-        __syncwarp();
-        const float4* U4 = &s_ring[warp][i % ST][0];
-        float2 wv = reinterpret_cast<const float2*>(&s_ring[warp][i % ST][16])[lane];
-#pragma unroll
-        for (int a4 = 0; a4 < 16; a4++) {
-          const float4 u = U4[a4];
-          upd2(wv.x, wv.y, ee[2 * a4].x, ee[2 * a4].y, u.x, u.y, nz);
-          upd2(wv.x, wv.y, ee[2 * a4 + 1].x, ee[2 * a4 + 1].y, u.z, u.w, nz);
-        }
-        W[(size_t)(first + i * WARPS) * 32 + lane] = wv;
-        __syncwarp();
-      }
-      cp_async_wait<0>();
-    }
-    __syncthreads();
   }
 }
 
-template <int WARPS>
-__global__ void __launch_bounds__(32 * WARPS, WARPS == 1 ? 16 : 2)
-ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+__global__ void __launch_bounds__(kSwThreads, 3) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
   int lo = 0, hi = b.count - 1;
   const int cta = blockIdx.x;
   while (lo < hi) {
@@ -205,43 +236,45 @@ ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
     if (b.d[mid].tile0 <= cta) lo = mid;
     else hi = mid - 1;
   }
-  sweep_tile<WARPS>(b.d[lo], cta - b.d[lo].tile0, nz);
+  sweep_rows(b.d[lo], cta - b.d[lo].tile0, nz);
 }
 
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
-  const int64_t ntiles = (nrow + 31) / 32;
-  return (size_t)ntiles * (size_t)n * 32 * sizeof(float);
+  const int64_t rows = (nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps) * (32 * kSweepWarps);
+  return (size_t)rows * (size_t)n * sizeof(float);
 }
 
-size_t ef_ut2_bytes(int64_t n) { return (size_t)n * (size_t)n * sizeof(float) + (size_t)n * sizeof(float); }
+size_t ef_u_prepared_bytes(int64_t n) { return (size_t)n * (size_t)n * sizeof(float) + (size_t)n * sizeof(float); }
 
-int launch_build_ut2(const float* U, int64_t n, float* UT2, float* diagU, cudaStream_t stream) {
+int launch_prepare_u(const float* U, int64_t n, float* out, cudaStream_t stream) {
   if (n % 32) return 2;
-  dim3 grid((unsigned)(n / 32), (unsigned)(n / 32));
-  build_ut2_kernel<<<grid, 256, 0, stream>>>(U, (int)n, UT2, diagU);
+  const size_t n4 = (size_t)n * n / 4;
+  const int grid = (int)std::min<size_t>((n4 + 255) / 256, (size_t)148 * 8);
+  prepare_u_kernel<<<grid, 256, 0, stream>>>(U, (int)n, out);
   note_launch();
   return 0;
 }
 
-int launch_ef_sweep_batch(const SweepBatch& b, int total_tiles, int warps, cudaStream_t stream) {
-  if (b.count == 0 || total_tiles == 0) return 0;
-  if (warps == 1) ef_sweep_batch_kernel<1><<<total_tiles, 32, 0, stream>>>(b, -0.0f);
-  else ef_sweep_batch_kernel<8><<<total_tiles, 256, 0, stream>>>(b, -0.0f);
+int sweep_ctas(int64_t nrow) { return (int)((nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps)); }
+
+int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream) {
+  if (b.count == 0 || total_ctas == 0) return 0;
+  ef_sweep_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
   note_launch();
   return 0;
 }
 
-bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* ut2,
+bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
                 const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d) {
   int sbw, lo, hi;
   bool has_min;
   if (!grid_spec(type, &sbw, &lo, &hi, &has_min)) return false;
   d->x = x;
   d->order = order;
-  d->ut2 = ut2;
+  d->u = u_prep;
   d->dl = dl;
   d->ml = has_min ? ml : nullptr;
-  d->work = (float2*)work;
+  d->work = (float*)work;
   d->codes = codes;
   d->wout = wcur;
   d->nrow = (int)nrow;
@@ -253,16 +286,13 @@ bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* or
   return true;
 }
 
-int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order,
-                    const float* UT2, const float* diagU, const float* dl, const float* ml, void* work,
-                    int8_t* codes, float* wcur, cudaStream_t stream) {
-  (void)diagU;
+int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
+                    const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, cudaStream_t stream) {
   if (n % 256 || nrow <= 0) return 2;
   SweepBatch b;
   b.count = 1;
-  if (!sweep_desc(type, x, nrow, n, order, UT2, dl, ml, work, codes, wcur, &b.d[0])) return 1;
-  const int tiles = (int)((nrow + 31) / 32);
-  return launch_ef_sweep_batch(b, tiles, tiles >= 2 * 16 * 148 ? 1 : 8, stream);
+  if (!sweep_desc(type, x, nrow, n, order, u_prep, dl, ml, work, codes, wcur, &b.d[0])) return 1;
+  return launch_ef_sweep_batch(b, sweep_ctas(nrow), stream);
 }
 
 // ---------------------------------------------------------------------------- no-allocation sweep
@@ -296,14 +326,14 @@ static int noalloc_scratch(void** out) {
   return 0;
 }
 
-int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* UT2,
+int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
                             const float* dl, const float* ml, int8_t* codes, float* wcur, cudaStream_t stream) {
   if (ef_sweep_workspace_bytes(nrow, n) > kNoAllocScratchBytes) return 6;
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
-  // The sweep writes every working element of its tiles before reading it, so the array's
-  // previous contents need no clearing.
-  return launch_ef_sweep(type, x, nrow, n, order, UT2, UT2 + (size_t)n * n, dl, ml, scratch, codes, wcur, stream);
+  // The sweep writes every error before reading it, so the array's previous contents need
+  // no clearing.
+  return launch_ef_sweep(type, x, nrow, n, order, u_prep, dl, ml, scratch, codes, wcur, stream);
 }
 
 }  // namespace cpk

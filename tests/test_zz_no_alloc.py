@@ -1,6 +1,6 @@
 """cp_ef_sweep_noalloc: the error-feedback sweep for callers that cannot allocate device memory
 (their device memory belongs to another allocator, or they reach the library through an FFI
-that cannot hand it a scratch buffer).  It keeps its working rows in a fixed array inside the
+that cannot hand it a scratch buffer).  It keeps its per-row errors in a fixed array inside the
 library.  Checked through the C ABI against cp_ef_sweep, which takes a caller workspace: two
 calls in a row with different shapes and types must both give identical codes and
 compensated weights, and an oversized shape must be refused.
@@ -73,7 +73,7 @@ def test_noalloc_sweep_refuses_shapes_beyond_its_scratch():
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     L = nat.lib()
-    nrow, n = 4128, 1024   # ceil(4128/32)*32 * 1024 * 4 bytes = 16.1 MiB > 16 MiB
+    nrow, n = 4128, 1024   # ceil(4128/128)*128 * 1024 * 4 bytes = 16.5 MiB > 16 MiB
     dummy = torch.zeros(16, device="cuda")
     rc = L.cp_ef_sweep_noalloc(nat.TYPE_ID["Q2_K"], nat.ptr(dummy), nrow, n, nat.ptr(dummy), nat.ptr(dummy),
                                nat.ptr(dummy), nat.ptr(dummy), nat.ptr(dummy), None, nat.stream_ptr(torch))
