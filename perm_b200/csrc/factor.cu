@@ -50,13 +50,12 @@ __global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
 // column and updates the trailing triangle element-parallel; each inverse column step forms
 // the row dot products with four threads per row and a shuffle reduction.
 // A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
-__global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k, int S) {
+__global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k) {
   __shared__ double a[NB][NB + 1];
   __shared__ double piv[NB];
   const int t = threadIdx.x;
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.x];
-  const double* part = part_base(A, n);
   int* status = fb.status[blockIdx.x];
   if (*status) return;
   for (int i = t; i < NB * NB; i += 256) {
@@ -64,8 +63,6 @@ __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_consta
     double v = 0.0;
     if (c <= r) {
       v = A[(size_t)(k + r) * n + k + c];
-      if (S > 1)  // split update of this column block: subtract its partial products in order
-        for (int q = 0; q < S; q++) v -= part[((size_t)q * n + k + r) * NB + c];
     }
     a[r][c] = v;
   }
@@ -189,7 +186,7 @@ __device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, co
 // Left-looking Cholesky step j, before the diagonal factorisation:
 //   A[j:n, j:j+64] -= L[j:n, 0:j] * L[j:j+64, 0:j]^T        (one 64-row tile per CTA)
 // With S > 1 the K range is split over blockIdx.y and each CTA writes its partial product;
-// the diagonal kernel and the panel solve subtract the partials (in order) when they read.
+// chol_reduce_kernel then subtracts the partials from the block column in order.
 __global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.z];
@@ -215,23 +212,49 @@ __global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__
     }
 }
 
+// Split-K reduction of a Cholesky step's update: A[r][j+c] -= part_0 - ... - part_{S-1}, in
+// that order, for every row r >= j of the block column (rows of the diagonal tile only on or
+// below the diagonal).  256 threads, one 64-row tile per CTA, 16 elements a thread.
+__global__ void __launch_bounds__(256) chol_reduce_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+  const int n = fb.n;
+  double* __restrict__ A = fb.P[blockIdx.y];
+  if (*fb.status[blockIdx.y]) return;
+  const double* part = part_base(A, n);
+  const int r0 = j + blockIdx.x * 64;
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    const int rr = r0 + i / 64, c = i % 64;
+    if (rr >= n || rr < j + c) continue;
+    double v = A[(size_t)rr * n + j + c];
+    for (int q = 0; q < S; q++) v -= part[((size_t)q * n + rr) * NB + c];
+    A[(size_t)rr * n + j + c] = v;
+  }
+}
+
+// Split-K reduction of a triangular-inverse step: T rows = -(part_0 + ... + part_{S-1}).
+__global__ void __launch_bounds__(256) trinv_reduce_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+  const int n = fb.n;
+  double* __restrict__ Pw = fb.P[blockIdx.y];
+  double* __restrict__ T = Pw + (size_t)n * n;
+  if (*fb.status[blockIdx.y]) return;
+  const double* part = part_base(Pw, n);
+  const int base = j + NB;
+  const int r0 = base + blockIdx.x * 64;
+  const int m = min(64, n - r0);
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    const int rr = i / 64, c = i % 64;
+    if (rr >= m) continue;
+    double v = 0.0;
+    for (int q = 0; q < S; q++) v += part[((size_t)q * n + r0 - base + rr) * NB + c];
+    T[(size_t)(r0 - base + rr) * NB + c] = -v;
+  }
+}
+
 // Panel below the diagonal block: A[j+64:n, j:j+64] := A * inv(L_jj)^T (inverse on the diagonal).
-__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
   if (*fb.status[blockIdx.y]) return;
   const int r0 = j + 64 + blockIdx.x * 64;
-  if (S > 1) {  // finish this tile's split update before solving with it
-    const double* part = part_base(A, n);
-    for (int i = threadIdx.x; i < 64 * 64; i += 64) {
-      const int rr = r0 + i / 64, c = i % 64;
-      if (rr >= n) continue;
-      double v = A[(size_t)rr * n + j + c];
-      for (int q = 0; q < S; q++) v -= part[((size_t)q * n + rr) * NB + c];
-      A[(size_t)rr * n + j + c] = v;
-    }
-    __syncthreads();
-  }
   double acc[8][8];
   tile64<true>(A + (size_t)r0 * n + j, n, A + (size_t)j * n + j, n, n - r0, 64, 64, acc);
   __syncthreads();  // every CTA reads only its own rows of the panel, so in-place is safe
@@ -248,7 +271,7 @@ __global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ 
 // Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
 //   T = -Linv22 * L21          (rows below, into scratch; Linv22 is lower triangular)
 // With S > 1 the K range is split over blockIdx.y; partial products go to the partial-tile
-// scratch and trinv_apply forms T from them in order.
+// scratch and trinv_reduce_kernel forms T from them in order.
 __global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ Pw = fb.P[blockIdx.z];
@@ -277,7 +300,7 @@ __global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ Factor
 }
 
 //   L21 := T * inv(L_jj)   (inv(L_jj) already sits on the diagonal)
-__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
   double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
@@ -285,17 +308,6 @@ __global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
-  if (S > 1) {  // T rows of this tile = -(sum of the split partial products, in order)
-    const double* part = part_base(A, n);
-    for (int i = threadIdx.x; i < 64 * 64; i += 64) {
-      const int rr = i / 64, c = i % 64;
-      if (rr >= m) continue;
-      double v = 0.0;
-      for (int q = 0; q < S; q++) v += part[((size_t)q * n + r0 - base + rr) * NB + c];
-      T[(size_t)(r0 - base + rr) * NB + c] = -v;
-    }
-    __syncthreads();
-  }
   double acc[8][8];
   tile64<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, 64, 64, acc);
   const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
@@ -339,11 +351,15 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     if (j > 0) {
       chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
       note_launch();
+      if (S > 1) {
+        chol_reduce_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)cnt), 256, 0, stream>>>(fb, j, S);
+        note_launch();
+      }
     }
-    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j, S);
+    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j);
     note_launch();
     if (n - j - NB > 0) {
-      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
+      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
       note_launch();
     }
   }
@@ -354,7 +370,11 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     const int S = ksplit(n - j - NB);
     trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
     note_launch();
-    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
+    if (S > 1) {
+      trinv_reduce_kernel<<<dim3(tiles, (unsigned)cnt), 256, 0, stream>>>(fb, j, S);
+      note_launch();
+    }
+    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
     note_launch();
   }
   {
