@@ -169,7 +169,7 @@ typedef struct {
   int64_t nrow, n;
 } cp_block_job;
 int cp_grid_params_batch(const cp_block_job* jobs, int count, void* stream);   /* ef.py:87-127 */
-int cp_kquant_repack_batch(const cp_block_job* jobs, int count, void* stream); /* ef.py:130-176 */
+int cp_kquant_repack_batch(const cp_block_job* jobs, int count, void* stream); /* ef.py:130-176; codes 16-byte aligned */
 int cp_weighted_err_batch(const cp_block_job* jobs, int count, void* stream);  /* ef.py:298-301 */
 
 typedef struct {
@@ -184,7 +184,7 @@ typedef struct {
   float* w_out;         /* optional */
   void* workspace;      /* cp_ef_sweep_workspace_bytes(nrow, n) bytes, one per job */
 } cp_sweep_job;
-/* ef.py:197-216 for every job in one launch (a CTA per 32 rows of any job). */
+/* ef.py:197-216 for every job in one launch (a CTA per 128 rows of any job). */
 int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream);
 
 typedef struct {

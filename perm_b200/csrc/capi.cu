@@ -370,6 +370,7 @@ static int block_batch(int op, const cp_block_job* jobs, int count, void* stream
     if (j.nrow == 0) continue;
     const bool ok = op == 0 ? (j.raw && j.dl) : op == 1 ? (j.raw_out && j.codes) : (j.raw && j.x && j.err);
     if (!ok) return set_err(CP_ERR_ARG, "null pointer in a block job");
+    if (op == 1 && (((uintptr_t)j.codes) & 15)) return set_err(CP_ERR_ARG, "codes must be 16-byte aligned");
     cpk::SbDesc& d = b.d[b.count++];
     d.raw = j.raw;
     d.raw_w = j.raw_out;
@@ -383,7 +384,7 @@ static int block_batch(int op, const cp_block_job* jobs, int count, void* stream
     d.nsb = j.nrow * d.nsb_row;
     d.sb0 = total;
     d.type = j.ggml_type;
-    total += op == 2 ? (d.nsb + 15) / 16 : d.nsb;
+    total += (d.nsb + 15) / 16;   // 16 superblocks per CTA
   }
   return CP_OK;
 }

@@ -216,82 +216,97 @@ __global__ void __launch_bounds__(256) weighted_err_kernel(const uint8_t* __rest
 }
 
 // ---------------------------------------------------------------------------- grouped launches
-// One CTA of 256 threads per superblock; CTAs find their tensor in the descriptor table.
+// One CTA of 256 threads per 16 superblocks of one tensor; CTAs find their tensor in the
+// descriptor table.
+constexpr int kSbPerCta = 16;
 
+// Grid of superblocks [c*16, c*16 + 16): one thread per (superblock, sub-block), writes
+// coalesced across the CTA.
 template <int T>
-__device__ __forceinline__ void grid_sb(const SbDesc& t, int64_t sb) {
+__device__ __forceinline__ void grid_sb(const SbDesc& t, int64_t c) {
   constexpr int NS = (T == kQ4_K || T == kQ5_K) ? 8 : 16;
-  if (threadIdx.x < NS) {
+  const int k = threadIdx.x / NS, j = threadIdx.x % NS;
+  const int64_t sb = c * kSbPerCta + k;
+  if (k < kSbPerCta && sb < t.nsb) {
     float a, m;
-    grid_of<T>(t.raw + sb * block_bytes(T), threadIdx.x, a, m);
-    t.dl[sb * NS + threadIdx.x] = a;
-    if (t.ml) t.ml[sb * NS + threadIdx.x] = m;
+    grid_of<T>(t.raw + sb * block_bytes(T), j, a, m);
+    t.dl[sb * NS + j] = a;
+    if (t.ml) t.ml[sb * NS + j] = m;
   }
 }
 
+// Codes of superblocks [c*16, c*16 + 16) into their bit fields; scales and super-scales are
+// left as committed.  The 16 x 256 codes come in with one 16-byte load per thread.
 template <int T>
-__device__ __forceinline__ void repack_sb(const SbDesc& t, int64_t sb) {
-  __shared__ int8_t c[256];
-  c[threadIdx.x] = t.codes[sb * 256 + threadIdx.x];
+__device__ __forceinline__ void repack_sb(const SbDesc& t, int64_t c) {
+  __shared__ __align__(16) int8_t cs[kSbPerCta][256];
+  const int64_t sb0 = c * kSbPerCta;
+  const int nsb = (int)min((int64_t)kSbPerCta, t.nsb - sb0);
+  {
+    const int k = threadIdx.x >> 4, q = threadIdx.x & 15;
+    if (k < nsb) reinterpret_cast<uint4*>(cs[k])[q] = reinterpret_cast<const uint4*>(t.codes + (sb0 + k) * 256)[q];
+  }
   __syncthreads();
-  uint8_t* b = t.raw_w + sb * block_bytes(T);
   const int th = threadIdx.x;
-  if (T == kQ2_K) {
-    if (th < 64) {
-      const int h = th >> 5, l = th & 31;
-      const int8_t* s = c + h * 128 + l;
-      b[16 + th] = (uint8_t)((s[0] & 3) | ((s[32] & 3) << 2) | ((s[64] & 3) << 4) | ((s[96] & 3) << 6));
-    }
-  } else if (T == kQ3_K) {
-    if (th < 32) {
-      uint8_t m = 0;
-      for (int j = 0; j < 8; j++) m |= (uint8_t)((c[32 * j + th] + 4 > 3 ? 1 : 0) << j);
-      b[th] = m;
-    } else if (th < 96) {
-      const int q = th - 32, h = q >> 5, l = q & 31;
-      uint8_t v = 0;
-      for (int k = 0; k < 4; k++) {
-        int x = c[h * 128 + 32 * k + l] + 4;
-        x = x > 3 ? x - 4 : x;
-        v |= (uint8_t)((x & 3) << (2 * k));
+  for (int k = 0; k < nsb; k++) {
+    const int8_t* cc = cs[k];
+    uint8_t* b = t.raw_w + (sb0 + k) * block_bytes(T);
+    if (T == kQ2_K) {
+      if (th < 64) {
+        const int h = th >> 5, l = th & 31;
+        const int8_t* s = cc + h * 128 + l;
+        b[16 + th] = (uint8_t)((s[0] & 3) | ((s[32] & 3) << 2) | ((s[64] & 3) << 4) | ((s[96] & 3) << 6));
       }
-      b[32 + q] = v;
-    }
-  } else if (T == kQ4_K || T == kQ5_K) {
-    const int off = (T == kQ5_K) ? 48 : 16;
-    if (th < 128) {
-      const int cc = th >> 5, l = th & 31;
-      int lo = c[cc * 64 + l], hi = c[cc * 64 + 32 + l];
-      if (T == kQ5_K) {
-        lo = lo > 15 ? lo - 16 : lo;
-        hi = hi > 15 ? hi - 16 : hi;
+    } else if (T == kQ3_K) {
+      if (th < 32) {
+        uint8_t m = 0;
+        for (int j = 0; j < 8; j++) m |= (uint8_t)((cc[32 * j + th] + 4 > 3 ? 1 : 0) << j);
+        b[th] = m;
+      } else if (th < 96) {
+        const int q = th - 32, h = q >> 5, l = q & 31;
+        uint8_t v = 0;
+        for (int kk = 0; kk < 4; kk++) {
+          int x = cc[h * 128 + 32 * kk + l] + 4;
+          x = x > 3 ? x - 4 : x;
+          v |= (uint8_t)((x & 3) << (2 * kk));
+        }
+        b[32 + q] = v;
       }
-      b[off + th] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
-    } else if (T == kQ5_K && th < 160) {
-      const int l = th - 128;
-      uint8_t m = 0;
-      for (int cc = 0; cc < 4; cc++) {
-        m |= (uint8_t)((c[cc * 64 + l] > 15 ? 1 : 0) << (2 * cc));
-        m |= (uint8_t)((c[cc * 64 + 32 + l] > 15 ? 1 : 0) << (2 * cc + 1));
+    } else if (T == kQ4_K || T == kQ5_K) {
+      const int off = (T == kQ5_K) ? 48 : 16;
+      if (th < 128) {
+        const int g = th >> 5, l = th & 31;
+        int lo = cc[g * 64 + l], hi = cc[g * 64 + 32 + l];
+        if (T == kQ5_K) {
+          lo = lo > 15 ? lo - 16 : lo;
+          hi = hi > 15 ? hi - 16 : hi;
+        }
+        b[off + th] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+      } else if (T == kQ5_K && th < 160) {
+        const int l = th - 128;
+        uint8_t m = 0;
+        for (int g = 0; g < 4; g++) {
+          m |= (uint8_t)((cc[g * 64 + l] > 15 ? 1 : 0) << (2 * g));
+          m |= (uint8_t)((cc[g * 64 + 32 + l] > 15 ? 1 : 0) << (2 * g + 1));
+        }
+        b[16 + l] = m;
       }
-      b[16 + l] = m;
-    }
-  } else {
-    if (th < 128) {
-      const int h = th >> 6, r = th & 63, l = r & 31;
-      const int base = h * 128 + l;
-      b[th] = (r < 32) ? (uint8_t)(((c[base] + 32) & 0xF) | (((c[base + 64] + 32) & 0xF) << 4))
-                       : (uint8_t)(((c[base + 32] + 32) & 0xF) | (((c[base + 96] + 32) & 0xF) << 4));
-    } else if (th < 192) {
-      const int q = th - 128, h = q >> 5, l = q & 31;
-      const int base = h * 128 + l;
-      b[128 + q] = (uint8_t)(((c[base] + 32) >> 4) | (((c[base + 32] + 32) >> 4) << 2) |
-                             (((c[base + 64] + 32) >> 4) << 4) | (((c[base + 96] + 32) >> 4) << 6));
+    } else {
+      if (th < 128) {
+        const int h = th >> 6, r = th & 63, l = r & 31;
+        const int base = h * 128 + l;
+        b[th] = (r < 32) ? (uint8_t)(((cc[base] + 32) & 0xF) | (((cc[base + 64] + 32) & 0xF) << 4))
+                         : (uint8_t)(((cc[base + 32] + 32) & 0xF) | (((cc[base + 96] + 32) & 0xF) << 4));
+      } else if (th < 192) {
+        const int q = th - 128, h = q >> 5, l = q & 31;
+        const int base = h * 128 + l;
+        b[128 + q] = (uint8_t)(((cc[base] + 32) >> 4) | (((cc[base + 32] + 32) >> 4) << 2) |
+                               (((cc[base + 64] + 32) >> 4) << 4) | (((cc[base + 96] + 32) >> 4) << 6));
+      }
     }
   }
 }
 
-constexpr int kWerrSbPerCta = 16;
 
 // Weighted squared error of superblocks [c*16, c*16 + 16) of one tensor, one atomic per CTA.
 template <int T>
@@ -299,8 +314,8 @@ __device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t c) {
   constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
   const int i = threadIdx.x;
   double acc = 0.0;
-  const int64_t sb_end = min(t.nsb, (c + 1) * kWerrSbPerCta);
-  for (int64_t sb = c * kWerrSbPerCta; sb < sb_end; sb++) {
+  const int64_t sb_end = min(t.nsb, (c + 1) * kSbPerCta);
+  for (int64_t sb = c * kSbPerCta; sb < sb_end; sb++) {
     const uint8_t* b = t.raw + sb * block_bytes(T);
     float dl, ml;
     grid_of<T>(b, i / SW, dl, ml);
@@ -331,7 +346,7 @@ __global__ void __launch_bounds__(256) sb_batch_kernel(const __grid_constant__ S
     else hi = mid - 1;
   }
   const SbDesc& t = b.d[lo];
-  const int64_t sb = cta - t.sb0;
+  const int64_t sb = cta - t.sb0;   // index of the CTA's group of 16 superblocks
 #define CPK_SB_OP(T)                              \
   if (OP == 0) grid_sb<T>(t, sb);                 \
   else if (OP == 1) repack_sb<T>(t, sb);          \
