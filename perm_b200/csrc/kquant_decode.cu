@@ -309,18 +309,34 @@ __device__ __forceinline__ void repack_sb(const SbDesc& t, int64_t c) {
 
 
 // Weighted squared error of superblocks [c*16, c*16 + 16) of one tensor, one atomic per CTA.
+// The group's raw bytes and its sub-block (dl, ml) pairs are staged in shared memory once;
+// each thread then decodes one element per superblock.
 template <int T>
 __device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t c) {
   constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
+  constexpr int NS = 256 / SW;
+  constexpr int BB = block_bytes(T);
+  __shared__ uint8_t sraw[kSbPerCta * 210];
+  __shared__ float sdl[kSbPerCta][16], sml[kSbPerCta][16];
   const int i = threadIdx.x;
+  const int64_t sb0 = c * kSbPerCta;
+  const int nsb = (int)min((int64_t)kSbPerCta, t.nsb - sb0);
+  const uint8_t* src = t.raw + sb0 * BB;
+  for (int k = i; k < nsb * BB; k += 256) sraw[k] = src[k];
+  __syncthreads();
+  if (i < nsb * NS) {
+    const int k = i / NS, j = i % NS;
+    float a, m;
+    grid_of<T>(sraw + k * BB, j, a, m);
+    sdl[k][j] = a;
+    sml[k][j] = m;
+  }
+  __syncthreads();
   double acc = 0.0;
-  const int64_t sb_end = min(t.nsb, (c + 1) * kSbPerCta);
-  for (int64_t sb = c * kSbPerCta; sb < sb_end; sb++) {
-    const uint8_t* b = t.raw + sb * block_bytes(T);
-    float dl, ml;
-    grid_of<T>(b, i / SW, dl, ml);
-    float v = dl * (float)code_of<T>(b, i);
-    if (!(T == kQ3_K || T == kQ6_K)) v = v - ml;
+  for (int k = 0; k < nsb; k++) {
+    const int64_t sb = sb0 + k;
+    float v = sdl[k][i / SW] * (float)code_of<T>(sraw + k * BB, i);
+    if (!(T == kQ3_K || T == kQ6_K)) v = v - sml[k][i / SW];
     const float d = v - t.x[sb * 256 + i];
     const float wt = t.w ? t.w[(sb % t.nsb_row) * 256 + i] : 1.0f;
     acc += (double)(d * d * wt);
