@@ -4,6 +4,7 @@ on the device and runs its kernels a few times.
 
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
     sweep_layers  eight Qwen3-0.6B-shaped layers (56 tensors), grouped EF sweep
+    sweep_model   all 28 layers' EF tensors (196 tensors), the whole-model sweep launch
     fit      Q2_K imatrix fit of a 4096 x 4096 tensor
     factor   batched FP64 factorisation of 16 Hessians n = 1024 and 4 of n = 3072
     factor_model  the whole 0.6B model's 112 factorisations
@@ -53,6 +54,20 @@ def case_sweep(torch, reps):
     shapes = [(1024, 1024, "Q2_K", "h1024")] * 24 + [(1024, 3072, "Q3_K", "h3072")] * 8
     ms, upd = _sweep_case(torch, reps, shapes)
     return f"sweep: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s"
+
+
+def case_sweep_model(torch, reps):
+    """All 28 Qwen3-0.6B-shaped layers' EF tensors (196 tensors, 2688 CTAs), each layer with its
+    own four Hessians (112 factors, as in the whole-model encode): the whole-model sweep."""
+    shapes = []
+    for l in range(28):
+        shapes += [(2048, 1024, "Q2_K", f"qkv{l}"), (1024, 1024, "Q2_K", f"qkv{l}"), (1024, 1024, "Q2_K", f"qkv{l}"),
+                   (1024, 2048, "Q2_K", f"o{l}"), (3072, 1024, "Q2_K", f"gu{l}"), (3072, 1024, "Q2_K", f"gu{l}"),
+                   (1024, 3072, "Q3_K", f"d{l}")]
+    shapes.sort(key=lambda s: -s[1])
+    ms, upd = _sweep_case(torch, reps, shapes)
+    return (f"sweep_model: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s, "
+            f"{2 * upd / ms / 1e9:.2f} T fp32 lane-ops/s")
 
 
 def case_sweep_layers(torch, reps):
@@ -161,7 +176,7 @@ def case_xtx_f32(torch, reps):
     return case_xtx(torch, reps, "f32")
 
 
-CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
+CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):

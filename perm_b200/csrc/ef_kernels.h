@@ -5,14 +5,8 @@
 #include <cuda_runtime.h>
 
 namespace cpk {
-// A sweep CTA has kSweepWarps warps; each thread owns kSweepRowsPerThread rows (1: two rows
-// per thread ran 1.4x slower on B200, register-capped at 255 with fewer CTAs to balance).
+// Rows per sweep CTA = 32 * kSweepWarps.
 constexpr int kSweepWarps = 4;
-#ifndef CPK_SWEEP_RPT
-#define CPK_SWEEP_RPT 1
-#endif
-constexpr int kSweepRowsPerThread = CPK_SWEEP_RPT;
-constexpr int kSweepRowsPerCta = 32 * kSweepWarps * kSweepRowsPerThread;
 // One tensor of a grouped error-feedback sweep launch (CTAs [tile0, tile0 + sweep_ctas(nrow))).
 struct SweepDesc {
   const float* x;

@@ -65,60 +65,46 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 constexpr int kSwB = 64;      // columns per block
 constexpr int kSwJS = 8;      // earlier columns (jj) per ring stage
+constexpr int kSwST = 4;      // ring stages
 constexpr int kSwThreads = 32 * kSweepWarps;
 
-template <int RPT, int ST>
 struct SweepSmem {
-  __align__(16) float ud[kSwB][kSwB];                     // U[j0+a][j0+b], the block's diagonal block
-  float dg[kSwB];                                         // U[j0+a][j0+a]
-  int ord[kSwB];                                          // order[j0+a]
-  __align__(16) float ru[ST][kSwJS][kSwB];                // ring: U[jj][j0 .. j0+63]
-  __align__(16) float re[ST][kSweepWarps * RPT][kSwJS][32];  // ring: errors e_jj of the CTA's rows
+  __align__(16) float ud[kSwB][kSwB];                // ud[a][b] = U[j0+a][j0+b], the block's diagonal block
+  float dg[kSwB];                                    // U[j0+a][j0+a]
+  int ord[kSwB];                                     // order[j0+a]
+  __align__(16) float ru[kSwST][kSwJS][kSwB];        // ring: U[jj][j0 .. j0+63]
+  __align__(16) float re[kSwST][kSweepWarps][kSwJS][32];  // ring: errors e_jj of each warp's rows
 };
 
-// One CTA = kSweepWarps warps x RPT x 32 rows of one tensor: thread (warp w, lane l) owns
-// rows (cta*kSweepWarps*RPT + w*RPT + r)*32 + l for r < RPT.  With RPT = 2 every U value
-// loaded from shared memory serves two rows, and the panel runs two independent chains.
-template <int RPT>
+// One CTA = kSweepWarps x 32 rows of one tensor.
 __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz) {
-  constexpr int ST = RPT == 1 ? 4 : 3;   // ring stages (the ring of RPT = 2 holds twice the errors)
-  constexpr int TW = kSweepWarps * RPT;  // 32-row tiles per CTA
-  __shared__ SweepSmem<RPT, ST> sm;
+  __shared__ SweepSmem sm;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = t.n, nrow = t.nrow;
+  const int tile32 = cta * kSweepWarps + warp;
+  const int row = tile32 * 32 + lane;
+  const bool rv = row < nrow;
   const int sbw = t.sbw, lo = t.lo, hi = t.hi, nsub = n / sbw;
   const float* __restrict__ U = t.u;
   const float* __restrict__ diagU = t.u + (size_t)n * n;
-  const float* __restrict__ Ecta = t.work + (size_t)cta * TW * n * 32;
-  bool rv[RPT];
-  const float* xr[RPT];
-  const float* dlr[RPT];
-  const float* mlr[RPT];
-  int8_t* codes[RPT];
-  float* wout[RPT];
-  float* Erow[RPT];
-#pragma unroll
-  for (int r = 0; r < RPT; r++) {
-    const int tile32 = cta * TW + warp * RPT + r, row = tile32 * 32 + lane;
-    rv[r] = row < nrow;
-    const int rr = rv[r] ? row : 0;
-    xr[r] = t.x + (size_t)rr * n;
-    dlr[r] = t.dl + (size_t)rr * nsub;
-    mlr[r] = t.ml ? t.ml + (size_t)rr * nsub : nullptr;
-    codes[r] = t.codes + (size_t)row * n;
-    wout[r] = t.wout ? t.wout + (size_t)row * n : nullptr;
-    Erow[r] = t.work + (size_t)tile32 * n * 32 + lane;
-  }
+  float* __restrict__ E = t.work;                              // [tile32][n][32]
+  const float* __restrict__ Ecta = t.work + (size_t)cta * kSweepWarps * n * 32;
+  float* __restrict__ Erow = E + (size_t)tile32 * n * 32 + lane;
+  const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * n;
+  const float* __restrict__ dlr = t.dl + (size_t)(rv ? row : 0) * nsub;
+  const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * nsub : nullptr;
+  int8_t* __restrict__ codes = t.codes + (size_t)row * n;
+  float* __restrict__ wout = t.wout ? t.wout + (size_t)row * n : nullptr;
 
   for (int j0 = 0; j0 < n; j0 += kSwB) {
     __syncthreads();  // the previous block's readers of the shared buffers are done
     const int nst = j0 / kSwJS;
     // stage s = U rows jj in [s*JS, s*JS + JS) of this block's columns + the CTA's errors
-    // of those jj (16 + 8 * TW chunks of 16 bytes per jj)
+    // of those jj (16 + 8 * kSweepWarps = 48 chunks of 16 bytes per jj)
     auto issue = [&](int s) {
       if (s < nst) {
-        const int st = s % ST, jj0 = s * kSwJS;
-        for (int c = tid; c < kSwJS * (16 + 8 * TW); c += kSwThreads) {
+        const int st = s % kSwST, jj0 = s * kSwJS;
+        for (int c = tid; c < kSwJS * (16 + 8 * kSweepWarps); c += kSwThreads) {
           if (c < kSwJS * 16) {
             const int k = c >> 4, c4 = c & 15;
             cp_async16(&sm.ru[st][k][4 * c4], U + (size_t)(jj0 + k) * n + j0 + 4 * c4);
@@ -132,7 +118,7 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
       cp_async_commit();
     };
 #pragma unroll
-    for (int s = 0; s < ST - 1; s++) issue(s);
+    for (int s = 0; s < kSwST - 1; s++) issue(s);
     for (int i = tid; i < kSwB * kSwB / 4; i += kSwThreads) {
       const int a = i >> 4, c4 = i & 15;
       reinterpret_cast<float4*>(sm.ud[a])[c4] =
@@ -145,97 +131,83 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     __syncthreads();
 
     // 1. the block's working values, w = x[row, order[j0 + c]]
-    float w[RPT][kSwB];
+    float w[kSwB];
 #pragma unroll
-    for (int c = 0; c < kSwB; c++)
-#pragma unroll
-      for (int r = 0; r < RPT; r++) w[r][c] = rv[r] ? __ldg(xr[r] + sm.ord[c]) : 0.0f;
+    for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c]) : 0.0f;
 
     // 2. errors of every earlier column, ascending jj
     for (int s = 0; s < nst; s++) {
-      cp_async_wait<ST - 2>();
+      cp_async_wait<kSwST - 2>();
       __syncthreads();  // stage s landed for everyone; everyone is done with stage s - 1
-      issue(s + ST - 1);
-      const int st = s % ST;
+      issue(s + kSwST - 1);
+      const int st = s % kSwST;
 #pragma unroll
       for (int k = 0; k < kSwJS; k++) {
-        float e[RPT];
-#pragma unroll
-        for (int r = 0; r < RPT; r++) e[r] = sm.re[st][warp * RPT + r][k][lane];
+        const float e = sm.re[st][warp][k][lane];
         const float4* u4 = reinterpret_cast<const float4*>(sm.ru[st][k]);
 #pragma unroll
         for (int c4 = 0; c4 < kSwB / 4; c4++) {
           const float4 u = u4[c4];
-#pragma unroll
-          for (int r = 0; r < RPT; r++) {
-            upd2(w[r][4 * c4], w[r][4 * c4 + 1], e[r], e[r], u.x, u.y, nz);
-            upd2(w[r][4 * c4 + 2], w[r][4 * c4 + 3], e[r], e[r], u.z, u.w, nz);
-          }
+          upd2(w[4 * c4], w[4 * c4 + 1], e, e, u.x, u.y, nz);
+          upd2(w[4 * c4 + 2], w[4 * c4 + 3], e, e, u.z, u.w, nz);
         }
       }
     }
     cp_async_wait<0>();
 
     // 3. panel: the block's 64 dependent quantize/error steps, as four sub-panels of 16
-    // (a run-time loop).  Sub-panel p quantizes w[.][0..15] in order, each step followed by
-    // its updates of the later columns of the sub-panel; then the 16 errors update the
-    // block's remaining 16-column groups (ascending jj, packed); then w shifts down by 16
-    // registers so the next sub-panel again finds its columns in w[.][0..15].  Register
-    // indices stay compile-time and no update is computed that the reference does not make.
-    // Grid values are fetched two steps ahead.
+    // (a run-time loop).  Sub-panel p quantizes w[0..15] in order, each step followed by its
+    // updates of the later columns of the sub-panel; then the 16 errors update the block's
+    // remaining 16-column groups (ascending jj, packed); then w shifts down by 16 registers so
+    // the next sub-panel again finds its columns in w[0..15].  Register indices stay
+    // compile-time and no update is computed that the reference does not make.
+    // dl/ml of sub-panel p + 1 are fetched while sub-panel p runs
+    float pd[16], pm[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int sidx = sm.ord[i] / sbw;
+      pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
+      pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+    }
 #pragma unroll 1
     for (int p = 0; p < kSwB / 16; p++) {
       const int a0 = 16 * p;
-      float es[RPT][16];
-      float qd[RPT][2], qm[RPT][2];
+      float es[16];
+      float cd[16], cm[16];
 #pragma unroll
-      for (int i = 0; i < 2; i++) {
-        const int sidx = sm.ord[a0 + i] / sbw;
+      for (int i = 0; i < 16; i++) {
+        cd[i] = pd[i];
+        cm[i] = pm[i];
+      }
+      if (p + 1 < kSwB / 16) {
 #pragma unroll
-        for (int r = 0; r < RPT; r++) {
-          qd[r][i] = rv[r] ? __ldg(dlr[r] + sidx) : 0.0f;
-          qm[r][i] = (rv[r] && mlr[r]) ? __ldg(mlr[r] + sidx) : 0.0f;
+        for (int i = 0; i < 16; i++) {
+          const int sidx = sm.ord[a0 + 16 + i] / sbw;
+          pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
+          pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
         }
       }
 #pragma unroll
       for (int i = 0; i < 16; i++) {
         const int a = a0 + i, j = sm.ord[a];
-        float dlv[RPT], mlv[RPT];
-#pragma unroll
-        for (int r = 0; r < RPT; r++) {
-          dlv[r] = qd[r][i & 1];
-          mlv[r] = qm[r][i & 1];
+        const float dlv = cd[i], mlv = cm[i], wa = w[i];
+        int q = 0;
+        float e = 0.0f;
+        if (dlv != 0.0f) {
+          q = clampi(nint((wa + mlv) / dlv), lo, hi);
+          const float recon = dlv * (float)q - mlv;
+          e = (wa - recon) / sm.dg[a];
         }
-        if (i + 2 < 16) {
-          const int sidx = sm.ord[a + 2] / sbw;
-#pragma unroll
-          for (int r = 0; r < RPT; r++) {
-            qd[r][i & 1] = rv[r] ? __ldg(dlr[r] + sidx) : 0.0f;
-            qm[r][i & 1] = (rv[r] && mlr[r]) ? __ldg(mlr[r] + sidx) : 0.0f;
-          }
+        if (rv) {
+          codes[j] = (int8_t)q;
+          if (wout) wout[j] = wa;
         }
-        const float dinv = sm.dg[a];
+        Erow[(size_t)(j0 + a) * 32] = e;
+        es[i] = e;
 #pragma unroll
-        for (int r = 0; r < RPT; r++) {
-          const float wa = w[r][i];
-          int q = 0;
-          float e = 0.0f;
-          if (dlv[r] != 0.0f) {
-            q = clampi(nint((wa + mlv[r]) / dlv[r]), lo, hi);
-            const float recon = dlv[r] * (float)q - mlv[r];
-            e = (wa - recon) / dinv;
-          }
-          if (rv[r]) {
-            codes[r][j] = (int8_t)q;
-            if (wout[r]) wout[r][j] = wa;
-          }
-          Erow[r][(size_t)(j0 + a) * 32] = e;
-          es[r][i] = e;
-#pragma unroll
-          for (int b = i + 1; b < 16; b++) w[r][b] = w[r][b] - e * sm.ud[a][a0 + b];
-        }
+        for (int b = i + 1; b < 16; b++) w[b] = w[b] - e * sm.ud[a][a0 + b];
       }
-      // later 16-column groups g of the block (columns a0 + 16 g .. +15 are w[.][16 g ..])
+      // later 16-column groups g of the block (columns a0 + 16 g .. +15 are w[16 g ..])
 #pragma unroll
       for (int g = 1; g < 4; g++) {
         if (p + g < kSwB / 16) {
@@ -245,22 +217,18 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
 #pragma unroll
             for (int c2 = 0; c2 < 8; c2++) {
               const float2 u = u2[c2];
-#pragma unroll
-              for (int r = 0; r < RPT; r++)
-                upd2(w[r][16 * g + 2 * c2], w[r][16 * g + 2 * c2 + 1], es[r][i], es[r][i], u.x, u.y, nz);
+              upd2(w[16 * g + 2 * c2], w[16 * g + 2 * c2 + 1], es[i], es[i], u.x, u.y, nz);
             }
           }
         }
       }
 #pragma unroll
-      for (int c = 0; c < kSwB - 16; c++)
-#pragma unroll
-        for (int r = 0; r < RPT; r++) w[r][c] = w[r][c + 16];
+      for (int c = 0; c < kSwB - 16; c++) w[c] = w[c + 16];
     }
   }
 }
 
-__global__ void __launch_bounds__(kSwThreads, 2) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+__global__ void __launch_bounds__(kSwThreads, 3) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
   int lo = 0, hi = b.count - 1;
   const int cta = blockIdx.x;
   while (lo < hi) {
@@ -268,11 +236,11 @@ __global__ void __launch_bounds__(kSwThreads, 2) ef_sweep_batch_kernel(const __g
     if (b.d[mid].tile0 <= cta) lo = mid;
     else hi = mid - 1;
   }
-  sweep_rows<kSweepRowsPerThread>(b.d[lo], cta - b.d[lo].tile0, nz);
+  sweep_rows(b.d[lo], cta - b.d[lo].tile0, nz);
 }
 
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
-  const int64_t rows = (nrow + kSweepRowsPerCta - 1) / kSweepRowsPerCta * kSweepRowsPerCta;
+  const int64_t rows = (nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps) * (32 * kSweepWarps);
   return (size_t)rows * (size_t)n * sizeof(float);
 }
 
@@ -287,7 +255,7 @@ int launch_prepare_u(const float* U, int64_t n, float* out, cudaStream_t stream)
   return 0;
 }
 
-int sweep_ctas(int64_t nrow) { return (int)((nrow + kSweepRowsPerCta - 1) / kSweepRowsPerCta); }
+int sweep_ctas(int64_t nrow) { return (int)((nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps)); }
 
 int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream) {
   if (b.count == 0 || total_ctas == 0) return 0;
