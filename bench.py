@@ -431,23 +431,33 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
                                                           for v in host_h.values())
     d2h = sum(all_sizes) if rank == 0 else 0
     s = nat.stream_ptr(torch)
+    copy_stream = torch.cuda.Stream()
+    # the stored diagonal is exact float32 and the decoded H carries it unchanged, so the
+    # host copy gives act order and damping without reading H back
+    host_diag = {k: v[1].numpy().astype(np.float64) for k, v in host_h.items()}
 
     def step():
+        # Hessians first (the factorisations need only them), the weights on a copy stream
+        # that runs beside the factorisations; the fits wait for the weights
         for k, (h16, d32, hscale) in host_h.items():
             dh16, dd32, H = dev_h[k]
             dh16.copy_(h16, non_blocking=True)
             dd32.copy_(d32, non_blocking=True)
             nat.check(nat.lib().cp_hessian_decode(nat.ptr(dh16), nat.ptr(dd32), float(hscale), H.shape[0],
                                                   nat.ptr(H), s), "hessian_decode")
-        for j in jobs:
-            dev_w16[j.name].copy_(host_w[j.name], non_blocking=True)
-            j.x.copy_(dev_w16[j.name])
         hs = {k: dev_h[k][2] for k in wl.ef_keys}
-        diags = {k: torch.diagonal(h).cpu().numpy() for k, h in hs.items()}
         for j in jobs:
             if j.qw is not None:
-                j.qw.copy_(torch.diagonal(hs[j.hkey]).float())
-        enc.run(jobs, hs, diags, stats=True, outputs=outputs)
+                j.qw.copy_(dev_h[j.hkey][1])
+        copy_stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(copy_stream):
+            for j in jobs:
+                dev_w16[j.name].copy_(host_w[j.name], non_blocking=True)
+                j.x.copy_(dev_w16[j.name])
+            weights_ready = torch.cuda.Event()
+            weights_ready.record(copy_stream)
+        enc.run(jobs, hs, {k: host_diag[k] for k in wl.ef_keys}, stats=True, outputs=outputs,
+                inputs_event=weights_ready)
         if world > 1:
             bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
             if rank == 0:

@@ -145,12 +145,16 @@ class Encoder:
             redone.append(k)
         return redone
 
-    def run(self, jobs, hessians, diags=None, stats=True, outputs=None):
+    def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None):
         """factor() + encode() with the factorisations overlapped with the round-1 fits: the
         factor chains start on side streams, the fits (which need no U) go first on this
         stream, and the status words are read once at the end; tensors whose Hessian needed
-        damp escalation are encoded again with the escalated factor."""
+        damp escalation are encoded again with the escalated factor.  inputs_event: a CUDA
+        event after which the weights are ready (e.g. copies on another stream); the
+        factorisations, which need only the Hessians, do not wait for it."""
         factors = self.factor(hessians, diags, check=False)
+        if inputs_event is not None:
+            (self.stream if self.stream is not None else self.torch.cuda.current_stream()).wait_event(inputs_event)
         raws, st = self.encode(jobs, factors, stats=stats, outputs=outputs, factor_event=self._factor_done)
         redone = set(self.escalate(factors))
         if redone:
