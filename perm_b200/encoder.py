@@ -79,44 +79,55 @@ class Encoder:
         keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
         if not keys:
             return {}
+        sizes = sorted({int(hessians[k].shape[0]) for k in keys}, reverse=True)
+        groups = {n: [k for k in keys if int(hessians[k].shape[0]) == n] for n in sizes}
         sig = tuple((k, int(hessians[k].shape[0])) for k in keys)
         if getattr(self, "_fsig", None) != sig:
+            # per-key factor workspaces and one pinned staging row of act orders per size group
             self._fws = {k: torch.empty(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])), dtype=torch.uint8,
                                         device="cuda") for k in keys}
+            self._forder_host = {n: torch.empty((len(groups[n]), n), dtype=torch.int32).pin_memory() for n in sizes}
             self._fsig = sig
-        status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
-        out, jobs = {}, []
-        for i, k in enumerate(keys):
-            H = hessians[k]
-            n = int(H.shape[0])
-            diag = diags[k] if diags is not None and k in diags else torch.diagonal(H).cpu().numpy()
-            order = np.argsort(-diag) if self.act_order else np.arange(n)
-            mean_diag = float(np.mean(np.asarray(diag, np.float64)[order]))
-            base = mean_diag if mean_diag > 0.0 else 1.0
-            od = torch.from_numpy(order.astype(np.int32)).to("cuda")
-            U = torch.empty((n, n), dtype=torch.float32, device="cuda")
-            jobs.append(nat.FactorJob(H.data_ptr(), n, od.data_ptr(), float(self.damp * base + 1e-8), U.data_ptr(),
-                                      self._fws[k].data_ptr(), status[i:i + 1].data_ptr()))
-            out[k] = Factor(U, order, od, self.damp)
-        # each size group is one chain of batched steps; the groups run side by side
-        main = self.stream if self.stream is not None else torch.cuda.current_stream()
-        sizes = sorted({int(hessians[k].shape[0]) for k in keys}, reverse=True)
         if getattr(self, "_fstreams", None) is None or len(self._fstreams) < len(sizes):
             self._fstreams = [torch.cuda.Stream(priority=self.factor_priority) for _ in range(max(4, len(sizes)))]
-        for k in keys:
-            f = out[k]
-            f.ut2 = torch.empty(L.cp_ef_u_bytes(int(f.U.shape[0])) // 4, dtype=torch.float32, device="cuda")
+        main = self.stream if self.stream is not None else torch.cuda.current_stream()
+        status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
+        slot = {k: i for i, k in enumerate(keys)}
         ready = torch.cuda.Event()
         ready.record(main)
+        out = {}
         self._factor_done = {}
+        # Each size group is one chain of batched steps on its own stream; the largest (the
+        # critical path) is prepared and launched first, so its chain starts while the host
+        # still prepares the smaller ones.
         for gi, n in enumerate(sizes):
+            grp = groups[n]
             st = self._fstreams[gi]
             st.wait_event(ready)
             sp = nat.stream_ptr(torch, st)
-            grp = [(i, k) for i, k in enumerate(keys) if int(hessians[k].shape[0]) == n]
-            arr = nat.job_array(nat.FactorJob, [jobs[i] for i, _ in grp])
+            oh = self._forder_host[n]
+            ohn = oh.numpy()
+            shifts = []
+            for r, k in enumerate(grp):
+                diag = diags[k] if diags is not None and k in diags else torch.diagonal(hessians[k]).cpu().numpy()
+                order = np.argsort(-diag) if self.act_order else np.arange(n)
+                ohn[r] = order
+                mean_diag = float(np.mean(np.asarray(diag, np.float64)[order]))
+                shifts.append(float(self.damp * (mean_diag if mean_diag > 0.0 else 1.0) + 1e-8))
+            with torch.cuda.stream(st):
+                od = oh.to("cuda", non_blocking=True)
+                Ug = torch.empty((len(grp), n, n), dtype=torch.float32, device="cuda")
+                ut2g = torch.empty((len(grp), L.cp_ef_u_bytes(n) // 4), dtype=torch.float32, device="cuda")
+            for t_ in (od, Ug, ut2g):   # also read on the main stream (sweeps)
+                t_.record_stream(main)
+            jobs = []
+            for r, k in enumerate(grp):
+                jobs.append(nat.FactorJob(hessians[k].data_ptr(), n, od[r].data_ptr(), shifts[r], Ug[r].data_ptr(),
+                                          self._fws[k].data_ptr(), status[slot[k]:slot[k] + 1].data_ptr()))
+                out[k] = Factor(Ug[r], ohn[r].astype(np.int64), od[r], self.damp, ut2g[r])
+            arr = nat.job_array(nat.FactorJob, jobs)
             nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
-            for _, k in grp:
+            for k in grp:
                 nat.check(L.cp_ef_prepare_u(nat.ptr(out[k].U), n, nat.ptr(out[k].ut2), sp), "prepare_u")
             done = torch.cuda.Event()
             done.record(st)
