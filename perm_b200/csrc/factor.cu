@@ -47,8 +47,8 @@ __global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
 // inverse, written in place of the block.  Nothing after this step needs L11 itself: the
 // panel below is solved with inv(L11) and the diagonal blocks of L^-1 are exactly these
 // inverses.  256 threads, block in shared memory: each Cholesky column step scales the
-// column and updates the trailing triangle element-parallel; each inverse column step forms
-// the row dot products with four threads per row and a shuffle reduction.
+// column and updates the trailing triangle with four threads per row; each inverse column
+// step forms the row dot products with four threads per row and a shuffle reduction.
 // A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
 __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k) {
   __shared__ double a[NB][NB + 1];
@@ -78,9 +78,12 @@ __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_consta
     const int m = NB - 1 - j;
     if (t < m) a[j + 1 + t][j] /= sq;
     __syncthreads();
-    for (int idx = t; idx < m * m; idx += 256) {
-      const int r = j + 1 + idx / m, c = j + 1 + idx % m;
-      if (c <= r) a[r][c] = fma(-a[r][j], a[c][j], a[r][c]);
+    {  // trailing triangle: row t / 4, columns j+1 + (t % 4) + 4i up to the diagonal
+      const int r = t >> 2, q = t & 3;
+      if (r > j) {
+        const double arj = a[r][j];
+        for (int c = j + 1 + q; c <= r; c += 4) a[r][c] = fma(-arj, a[c][j], a[r][c]);
+      }
     }
     __syncthreads();
   }
