@@ -130,10 +130,18 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     }
     __syncthreads();
 
-    // 1. the block's working values, w = x[row, order[j0 + c]]
+    // 1. the block's working values, w = x[row, order[j0 + c]], and the grid values of the
+    // panel's first 16 columns (they land while step 2 runs)
     float w[kSwB];
 #pragma unroll
     for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c]) : 0.0f;
+    float pd[16], pm[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int sidx = sm.ord[i] / sbw;
+      pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
+      pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+    }
 
     // 2. errors of every earlier column, ascending jj
     for (int s = 0; s < nst; s++) {
@@ -162,13 +170,6 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     // the next sub-panel again finds its columns in w[0..15].  Register indices stay
     // compile-time and no update is computed that the reference does not make.
     // dl/ml of sub-panel p + 1 are fetched while sub-panel p runs
-    float pd[16], pm[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const int sidx = sm.ord[i] / sbw;
-      pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
-      pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
-    }
 #pragma unroll 1
     for (int p = 0; p < kSwB / 16; p++) {
       const int a0 = 16 * p;
