@@ -372,9 +372,17 @@ def gpu_arm(args, rank, world, local_rank):
                "unit": "FP64 TFLOP/s (nominal peak)", "work": "(2/3) n^3 per factorisation"}
     if alu.get("peak"):
         alu["frac"] = alu["achieved"] / alu["peak"]
+    traffic = None
+    if dom == "sweep":
+        # DRAM bytes of one sweep launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) of
+        # the second step's first sweep launch of this default workload on one B200 measured
+        # 137.6 GB for 425.1 G ordered updates, 0.3237 bytes per update; per launch of this
+        # rank = that rate x this rank's updates per round
+        traffic = 0.3237 * alg["sweep_updates"] / max(1.0, nl)
     roofline = {"kernel": {"fit": "kquant fit+pack", "sweep": "ef_sweep", "factor": "fp64 factor"}[dom],
                 "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                "frac": (gbs / hbm) if gbs is not None else None, "traffic": None,
+                "frac": (gbs / hbm) if gbs is not None else None, "traffic": traffic,
+                "traffic_unit": "bytes per launch (ncu, scaled by this rank's updates)",
                 "peak_source": f"{peak_src} hbm_gbs", "launches_per_step": nl,
                 "ms_per_step": kms, "alu": alu,
                 "classes_ms_per_step": {c: round(per_step[c][0], 4) for c in per_step}}
