@@ -167,6 +167,9 @@ typedef struct {
   float* ml;
   double* err;          /* weighted error: the call ADDS this tensor's sum to *err */
   int64_t nrow, n;
+  int64_t grid_pitch;   /* grid params: 0 writes dl, ml as [nrow, n/sbw]; > 0 column-major,
+                           element (row, sub-block s) at s * grid_pitch + row (the layout a
+                           cp_sweep_job with pitch = grid_pitch reads) */
 } cp_block_job;
 int cp_grid_params_batch(const cp_block_job* jobs, int count, void* stream);   /* ef.py:87-127 */
 int cp_kquant_repack_batch(const cp_block_job* jobs, int count, void* stream); /* ef.py:130-176; codes 16-byte aligned */
@@ -183,8 +186,24 @@ typedef struct {
   int8_t* codes;
   float* w_out;         /* optional */
   void* workspace;      /* cp_ef_sweep_workspace_bytes(nrow, n) bytes, one per job */
+  int64_t pitch;        /* 0: x, codes, w_out row-major [nrow, n] and dl, ml [nrow, n/sbw].
+                           >= cp_ef_sweep_rows(nrow): all five column-major, element (row, col)
+                           at col * pitch + row; the sweep's one-lane-per-row accesses then
+                           coalesce (cp_transpose_batch converts) */
 } cp_sweep_job;
 /* ef.py:197-216 for every job in one launch (a CTA per 128 rows of any job). */
+/* Rows a tensor's sweep CTAs cover: nrow rounded up to 128, the smallest column-major pitch. */
+int64_t cp_ef_sweep_rows(int64_t nrow);
+
+/* Grouped transposes (layout conversions around the column-major sweep): dst[c * dst_ld + r]
+ * = src[r * src_ld + c] for r < rows, c < cols; elements of elem_bytes = 1 or 4. */
+typedef struct {
+  const void* src;
+  void* dst;
+  int64_t rows, cols, src_ld, dst_ld;
+  int32_t elem_bytes;
+} cp_transpose_job;
+int cp_transpose_batch(const cp_transpose_job* jobs, int count, void* stream);
 int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream);
 
 typedef struct {

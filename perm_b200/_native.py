@@ -32,14 +32,20 @@ class BlockJob(ctypes.Structure):
     _fields_ = [("ggml_type", ctypes.c_int), ("raw", ctypes.c_void_p), ("raw_out", ctypes.c_void_p),
                 ("codes", ctypes.c_void_p), ("x", ctypes.c_void_p), ("w", ctypes.c_void_p),
                 ("dl", ctypes.c_void_p), ("ml", ctypes.c_void_p), ("err", ctypes.c_void_p),
-                ("nrow", ctypes.c_int64), ("n", ctypes.c_int64)]
+                ("nrow", ctypes.c_int64), ("n", ctypes.c_int64), ("grid_pitch", ctypes.c_int64)]
 
 
 class SweepJob(ctypes.Structure):
     _fields_ = [("ggml_type", ctypes.c_int), ("x", ctypes.c_void_p), ("nrow", ctypes.c_int64),
                 ("n", ctypes.c_int64), ("order", ctypes.c_void_p), ("u_prepared", ctypes.c_void_p),
                 ("dl", ctypes.c_void_p), ("ml", ctypes.c_void_p), ("codes", ctypes.c_void_p),
-                ("w_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p)]
+                ("w_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("pitch", ctypes.c_int64)]
+
+
+class TransposeJob(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("rows", ctypes.c_int64),
+                ("cols", ctypes.c_int64), ("src_ld", ctypes.c_int64), ("dst_ld", ctypes.c_int64),
+                ("elem_bytes", ctypes.c_int32)]
 
 
 def job_array(cls, items):
@@ -104,6 +110,8 @@ def lib():
         "cp_ef_sweep_batch": ([P, I, P], I),
         "cp_factor_u_batch": ([P, I, P], I),
         "cp_ef_sweep_noalloc": ([I, P, I64, I64, P, P, P, P, P, P, P], I),
+        "cp_ef_sweep_rows": ([I64], I64),
+        "cp_transpose_batch": ([P, I, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

@@ -9,6 +9,7 @@
 #include "kq_common.cuh"
 #include "kquant_kernels.h"
 #include "xtx_kernels.h"
+#include "layout_kernels.h"
 
 namespace {
 
@@ -370,6 +371,7 @@ static int block_batch(int op, const cp_block_job* jobs, int count, void* stream
     if (j.nrow == 0) continue;
     const bool ok = op == 0 ? (j.raw && j.dl) : op == 1 ? (j.raw_out && j.codes) : (j.raw && j.x && j.err);
     if (!ok) return set_err(CP_ERR_ARG, "null pointer in a block job");
+    if (op == 0 && j.grid_pitch != 0 && j.grid_pitch < j.nrow) return set_err(CP_ERR_ARG, "grid_pitch < nrow");
     if (op == 1 && (((uintptr_t)j.codes) & 15)) return set_err(CP_ERR_ARG, "codes must be 16-byte aligned");
     cpk::SbDesc& d = b.d[b.count++];
     d.raw = j.raw;
@@ -383,6 +385,7 @@ static int block_batch(int op, const cp_block_job* jobs, int count, void* stream
     d.nsb_row = j.n / 256;
     d.nsb = j.nrow * d.nsb_row;
     d.sb0 = total;
+    d.gpitch = op == 0 ? j.grid_pitch : 0;
     d.type = j.ggml_type;
     total += (d.nsb + 15) / 16;   // 16 superblocks per CTA
   }
@@ -427,9 +430,52 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
       return set_err(CP_ERR_TYPE, "cp_ef_sweep_batch: unsupported type");
     if (d.ml == nullptr && (j.ggml_type == cpk::kQ2_K || j.ggml_type == cpk::kQ4_K || j.ggml_type == cpk::kQ5_K))
       return set_err(CP_ERR_ARG, "ml is required for Q2_K/Q4_K/Q5_K");
+    if (j.pitch != 0 && j.pitch < cpk::sweep_rows_padded(j.nrow))
+      return set_err(CP_ERR_ARG, "cp_ef_sweep_batch: pitch < cp_ef_sweep_rows(nrow)");
+    if (j.pitch > (int64_t)1 << 31) return set_err(CP_ERR_SHAPE, "cp_ef_sweep_batch: pitch too large");
+    d.pitch = (int)j.pitch;
     d.tile0 = tiles;
     tiles += cpk::sweep_ctas(j.nrow);
     b.count++;
+  }
+  return CP_OK;
+}
+
+int64_t cp_ef_sweep_rows(int64_t nrow) { return nrow > 0 ? cpk::sweep_rows_padded(nrow) : 0; }
+
+int cp_transpose_batch(const cp_transpose_job* jobs, int count, void* stream) {
+  if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
+  cudaStream_t s = (cudaStream_t)stream;
+  static thread_local cpk::TrBatch b;
+  for (int eb : {4, 1}) {
+    b.count = 0;
+    int64_t tiles = 0;
+    for (int i = 0; i <= count; i++) {
+      const bool flush = (i == count) || b.count == cpk::kTrBatchMax;
+      if (flush && b.count) {
+        ProfScope ps(kProfOther, s);
+        if (int rc = check_rc(cpk::launch_transpose_batch(b, eb, tiles, s), "cp_transpose_batch")) return rc;
+        b.count = 0;
+        tiles = 0;
+      }
+      if (i == count) break;
+      const cp_transpose_job& j = jobs[i];
+      if (j.elem_bytes != 1 && j.elem_bytes != 4) return set_err(CP_ERR_ARG, "elem_bytes must be 1 or 4");
+      if (j.elem_bytes != eb || j.rows == 0 || j.cols == 0) continue;
+      if (j.rows < 0 || j.cols < 0 || j.src_ld < j.cols || j.dst_ld < j.rows)
+        return set_err(CP_ERR_SHAPE, "cp_transpose_batch: bad rows, cols or leading dimensions");
+      if (!j.src || !j.dst) return set_err(CP_ERR_ARG, "null pointer in a transpose job");
+      cpk::TrDesc& d = b.d[b.count++];
+      d.src = j.src;
+      d.dst = j.dst;
+      d.rows = j.rows;
+      d.cols = j.cols;
+      d.src_ld = j.src_ld;
+      d.dst_ld = j.dst_ld;
+      d.tiles_c = (j.cols + 31) / 32;
+      d.tile0 = tiles;
+      tiles += cpk::transpose_tiles(j.rows, j.cols);
+    }
   }
   return CP_OK;
 }

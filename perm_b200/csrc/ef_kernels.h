@@ -18,14 +18,20 @@ struct SweepDesc {
   int8_t* codes;
   float* wout;        // null in the last round
   int nrow, n, sbw, lo, hi, tile0;
+  // 0: x, codes, wout row-major [nrow][n] and dl, ml [nrow][n/sbw].  > 0: all five
+  // column-major with this many elements from one column to the next (rows contiguous, so the
+  // sweep's lane-per-row accesses coalesce); pitch >= the rows the tensor's CTAs cover.
+  int pitch;
 };
-constexpr int kSweepBatchMax = 320;  // 88-byte descriptors: the table travels as a kernel parameter
+constexpr int kSweepBatchMax = 320;  // 96-byte descriptors: the table travels as a kernel parameter
 struct SweepBatch {
   int count;
   SweepDesc d[kSweepBatchMax];
 };
 bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,
                 const float* dl, const float* ml, void* work, int8_t* codes, float* wcur, SweepDesc* d);
+// Rows a tensor's sweep CTAs cover (nrow rounded up to 32 * kSweepWarps): the smallest pitch.
+int64_t sweep_rows_padded(int64_t nrow);
 int sweep_ctas(int64_t nrow);
 int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream);
 // Sweep with its working rows in a fixed per-device array (no caller workspace).

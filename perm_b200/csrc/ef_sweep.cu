@@ -90,11 +90,15 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
   float* __restrict__ E = t.work;                              // [tile32][n][32]
   const float* __restrict__ Ecta = t.work + (size_t)cta * kSweepWarps * n * 32;
   float* __restrict__ Erow = E + (size_t)tile32 * n * 32 + lane;
-  const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * n;
-  const float* __restrict__ dlr = t.dl + (size_t)(rv ? row : 0) * nsub;
-  const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * nsub : nullptr;
-  int8_t* __restrict__ codes = t.codes + (size_t)row * n;
-  float* __restrict__ wout = t.wout ? t.wout + (size_t)row * n : nullptr;
+  // element (row, column) of x, codes and wout sits at row * rs + column * cs (grid arrays:
+  // row * rsg + sub-block * cs); the column-major layout makes each warp access one 128-byte
+  // (or 32-byte for codes) segment
+  const int64_t cs = t.pitch ? t.pitch : 1, rs = t.pitch ? 1 : n, rsg = t.pitch ? 1 : nsub;
+  const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * rs;
+  const float* __restrict__ dlr = t.dl + (size_t)(rv ? row : 0) * rsg;
+  const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * rsg : nullptr;
+  int8_t* __restrict__ codes = t.codes + (size_t)row * rs;
+  float* __restrict__ wout = t.wout ? t.wout + (size_t)row * rs : nullptr;
 
   for (int j0 = 0; j0 < n; j0 += kSwB) {
     __syncthreads();  // the previous block's readers of the shared buffers are done
@@ -134,13 +138,13 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     // panel's first 16 columns (they land while step 2 runs)
     float w[kSwB];
 #pragma unroll
-    for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c]) : 0.0f;
+    for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c] * cs) : 0.0f;
     float pd[16], pm[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) {
       const int sidx = sm.ord[i] / sbw;
-      pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
-      pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+      pd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
+      pm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
     }
 
     // 2. errors of every earlier column, ascending jj
@@ -184,8 +188,8 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
 #pragma unroll
         for (int i = 0; i < 16; i++) {
           const int sidx = sm.ord[a0 + 16 + i] / sbw;
-          pd[i] = rv ? __ldg(dlr + sidx) : 0.0f;
-          pm[i] = (rv && mlr) ? __ldg(mlr + sidx) : 0.0f;
+          pd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
+          pm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
         }
       }
 #pragma unroll
@@ -200,8 +204,8 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
           e = (wa - recon) / sm.dg[a];
         }
         if (rv) {
-          codes[j] = (int8_t)q;
-          if (wout) wout[j] = wa;
+          codes[j * cs] = (int8_t)q;
+          if (wout) wout[j * cs] = wa;
         }
         Erow[(size_t)(j0 + a) * 32] = e;
         es[i] = e;
@@ -256,6 +260,10 @@ int launch_prepare_u(const float* U, int64_t n, float* out, cudaStream_t stream)
   return 0;
 }
 
+int64_t sweep_rows_padded(int64_t nrow) {
+  return (nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps) * (32 * kSweepWarps);
+}
+
 int sweep_ctas(int64_t nrow) { return (int)((nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps)); }
 
 int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream) {
@@ -278,6 +286,7 @@ bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* or
   d->work = (float*)work;
   d->codes = codes;
   d->wout = wcur;
+  d->pitch = 0;
   d->nrow = (int)nrow;
   d->n = (int)n;
   d->sbw = sbw;

@@ -230,8 +230,13 @@ __device__ __forceinline__ void grid_sb(const SbDesc& t, int64_t c) {
   if (k < kSbPerCta && sb < t.nsb) {
     float a, m;
     grid_of<T>(t.raw + sb * block_bytes(T), j, a, m);
-    t.dl[sb * NS + j] = a;
-    if (t.ml) t.ml[sb * NS + j] = m;
+    int64_t o = sb * NS + j;
+    if (t.gpitch) {   // column-major: (row, sub-block s) at s * gpitch + row
+      const int64_t row = sb / t.nsb_row, sub = (sb % t.nsb_row) * NS + j;
+      o = sub * t.gpitch + row;
+    }
+    t.dl[o] = a;
+    if (t.ml) t.ml[o] = m;
   }
 }
 

@@ -45,9 +45,10 @@ struct SbDesc {
   float* ml;
   double* err;
   int64_t nsb, nsb_row, sb0;
+  int64_t gpitch;       // grid output: 0 row-major [nrow][n/sbw], else column-major with this pitch
   int type;
 };
-constexpr int kSbBatchMax = 320;
+constexpr int kSbBatchMax = 300;  // 104-byte descriptors in the kernel parameters (32 KB limit)
 struct SbBatch {
   int count;
   SbDesc d[kSbBatchMax];

@@ -1,0 +1,21 @@
+// Internal launcher declarations for the grouped transposes.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace cpk {
+// One transpose of a grouped launch: dst[c * dst_ld + r] = src[r * src_ld + c], CTAs
+// [tile0, tile0 + transpose_tiles(rows, cols)) over 32 x 32 tiles (tiles_c tiles per row).
+struct TrDesc {
+  const void* src;
+  void* dst;
+  int64_t rows, cols, src_ld, dst_ld, tile0, tiles_c;
+};
+constexpr int kTrBatchMax = 256;   // 64-byte descriptors in the kernel parameters
+struct TrBatch {
+  int count;
+  TrDesc d[kTrBatchMax];
+};
+int64_t transpose_tiles(int64_t rows, int64_t cols);
+int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles, cudaStream_t stream);
+}  // namespace cpk

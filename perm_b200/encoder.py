@@ -54,13 +54,17 @@ class Encoder:
     sweeps as soon as that size's factors are done instead of after all of them (measured
     slower on the 0.6B model: the sweeps then slow the factor chain that gates the rest).
     factor_priority: CUDA stream priority of the factorisation streams (-1 high, 0 normal;
-    high lets the latency-bound factor chain run ahead of the round-1 fits)."""
+    high lets the latency-bound factor chain run ahead of the round-1 fits).
+    column_major: give the sweep its weights, grid, codes and compensated weights column-major
+    (one lane per row then reads and writes whole 128-byte segments), converting with grouped
+    transposes; False keeps everything row-major."""
 
     def __init__(self, n_iter=2, damp=0.01, act_order=True, stream=None, log=None, overlap_sweeps=False,
-                 factor_priority=-1):
+                 factor_priority=-1, column_major=True):
         self.torch = nat.torch_cuda()
         self.n_iter, self.damp, self.act_order = n_iter, damp, act_order
         self.overlap_sweeps, self.factor_priority = overlap_sweeps, factor_priority
+        self.column_major = column_major
         self.stream = stream
         self.log = log
         self._ws = None
@@ -180,24 +184,30 @@ class Encoder:
         carved from a few flat buffers that are reused while the job shapes stay the same."""
         torch = self.torch
         L = nat.lib()
-        key = tuple((j.name, j.ttype, j.mode, int(j.x.shape[0]), int(j.x.shape[1])) for j in jobs)
+        cm = self.column_major
+        key = (cm,) + tuple((j.name, j.ttype, j.mode, int(j.x.shape[0]), int(j.x.shape[1])) for j in jobs)
         if getattr(self, "_arena_key", None) == key:
             return self._arena_views
-        sizes = {"codes": 0, "wcur": 0, "grid": 0, "work": 0, "base": 0}
+        sizes = {"codes": 0, "wcur": 0, "grid": 0, "work": 0, "base": 0, "xt": 0, "ct": 0, "wt": 0}
         plan = []
         for j in jobs:
             nrow, n = int(j.x.shape[0]), int(j.x.shape[1])
             ent = {}
             if j.mode == "EF":
                 sbw = nat.GRID[j.ttype][0]
+                R = int(L.cp_ef_sweep_rows(nrow)) if cm else nrow   # rows of the column-major layout
                 ent["codes"] = (sizes["codes"], nrow * n)
                 sizes["codes"] += _al(nrow * n)
                 ent["wcur"] = (sizes["wcur"], nrow * n)
                 sizes["wcur"] += _al(nrow * n)
-                ent["dl"] = (sizes["grid"], nrow * (n // sbw))
-                sizes["grid"] += _al(nrow * (n // sbw))
-                ent["ml"] = (sizes["grid"], nrow * (n // sbw))
-                sizes["grid"] += _al(nrow * (n // sbw))
+                ent["dl"] = (sizes["grid"], R * (n // sbw))
+                sizes["grid"] += _al(R * (n // sbw))
+                ent["ml"] = (sizes["grid"], R * (n // sbw))
+                sizes["grid"] += _al(R * (n // sbw))
+                if cm:
+                    for k in ("xt", "ct", "wt"):
+                        ent[k] = (sizes[k], R * n)
+                        sizes[k] += _al(R * n)
                 wb = L.cp_ef_sweep_workspace_bytes(nrow, n)
                 ent["work"] = (sizes["work"], wb // 4)
                 sizes["work"] += _al(wb // 4)
@@ -212,6 +222,9 @@ class Encoder:
             "grid": torch.empty(max(1, sizes["grid"]), dtype=torch.float32, device="cuda"),
             "work": torch.empty(max(1, sizes["work"]), dtype=torch.float32, device="cuda"),
             "base": torch.empty(max(1, sizes["base"]), dtype=torch.uint8, device="cuda"),
+            "xt": torch.empty(max(1, sizes["xt"]), dtype=torch.float32, device="cuda"),
+            "ct": torch.empty(max(1, sizes["ct"]), dtype=torch.int8, device="cuda"),
+            "wt": torch.empty(max(1, sizes["wt"]), dtype=torch.float32, device="cuda"),
         }
         views = []
         for j, ent in zip(jobs, plan):
@@ -219,7 +232,7 @@ class Encoder:
             v = {}
             for k, (off, cnt) in ent.items():
                 src = {"codes": "codes", "wcur": "wcur", "dl": "grid", "ml": "grid", "work": "work",
-                       "base": "base"}[k]
+                       "base": "base", "xt": "xt", "ct": "ct", "wt": "wt"}[k]
                 v[k] = self._arena_buf[src][off:off + cnt]
             views.append(v)
         self._arena_key, self._arena_views = key, views
@@ -257,6 +270,15 @@ class Encoder:
             arr = nat.job_array(nat.BlockJob, items)
             nat.check(fn(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
 
+        cm = self.column_major
+        pitch = {i: int(L.cp_ef_sweep_rows(int(jobs[i].x.shape[0]))) for i in ef_idx} if cm else {}
+
+        def transpose(items, what):  # items: (src, dst, rows, cols, src_ld, dst_ld, elem_bytes)
+            if not items:
+                return
+            arr = nat.job_array(nat.TransposeJob, [nat.TransposeJob(*it) for it in items])
+            nat.check(L.cp_transpose_batch(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
+
         def werr_items(idx_list, col, use_base=False):
             out = []
             for i in idx_list:
@@ -286,6 +308,10 @@ class Encoder:
                        werr_items([i for i, j in enumerate(jobs) if j.mode == "wRTN(attn0-diag)"], 1, True),
                        "weighted_err_batch")
         main = self.stream if self.stream is not None else torch.cuda.current_stream()
+        if cm:  # the sweep's weights column-major, once for every round
+            transpose([(nat.addr(jobs[i].x), nat.addr(views[i]["xt"]), int(jobs[i].x.shape[0]),
+                        int(jobs[i].x.shape[1]), int(jobs[i].x.shape[1]), pitch[i], 4) for i in ef_idx],
+                      "transpose x")
         for it in range(self.n_iter):
             if it > 0:
                 fit_batch([(jobs[i].ttype, views[i]["wcur"].view(jobs[i].x.shape), jobs[i].qw, raws[i])
@@ -296,7 +322,7 @@ class Encoder:
                 hm = nat.GRID[j.ttype][3]
                 grid.append(nat.BlockJob(TYPE_ID[j.ttype], nat.addr(raws[i]), None, None, None, None,
                                          nat.addr(views[i]["dl"]), nat.addr(views[i]["ml"]) if hm else None, None,
-                                         int(j.x.shape[0]), int(j.x.shape[1])))
+                                         int(j.x.shape[0]), int(j.x.shape[1]), pitch.get(i, 0)))
             block_call(L.cp_grid_params_batch, grid, "grid_params_batch")
             # The first round's sweeps go out per Hessian size as soon as that size's factors
             # (side streams, factor_event {n: event}) are done, smallest first, so they overlap
@@ -321,17 +347,28 @@ class Encoder:
                     j = jobs[i]
                     f = factors[j.hkey]
                     hm = nat.GRID[j.ttype][3]
-                    sw.append(nat.SweepJob(TYPE_ID[j.ttype], nat.addr(j.x), int(j.x.shape[0]), int(j.x.shape[1]),
+                    last = it + 1 == self.n_iter
+                    xs, cs_, ws = (("xt", "ct", "wt") if cm else ("x", "codes", "wcur"))
+                    sw.append(nat.SweepJob(TYPE_ID[j.ttype], nat.addr(j.x if xs == "x" else views[i][xs]),
+                                           int(j.x.shape[0]), int(j.x.shape[1]),
                                            nat.addr(f.order_dev), nat.addr(f.ut2), nat.addr(views[i]["dl"]),
-                                           nat.addr(views[i]["ml"]) if hm else None, nat.addr(views[i]["codes"]),
-                                           nat.addr(views[i]["wcur"]) if it + 1 < self.n_iter else None,
-                                           nat.addr(views[i]["work"])))
+                                           nat.addr(views[i]["ml"]) if hm else None, nat.addr(views[i][cs_]),
+                                           None if last else nat.addr(views[i][ws]),
+                                           nat.addr(views[i]["work"]), pitch.get(i, 0)))
                 if sw:
                     arr = nat.job_array(nat.SweepJob, sw)
                     nat.check(L.cp_ef_sweep_batch(ctypes.cast(arr, ctypes.c_void_p), len(sw), s), "ef_sweep_batch")
             if it == 0 and factor_event:
                 for n in factor_event:   # everything after this point needs every factor
                     main.wait_event(factor_event[n])
+            if cm:  # codes (and the next round's fit input) back to storage order
+                tr = []
+                for i in ef_idx:
+                    nrow, n = int(jobs[i].x.shape[0]), int(jobs[i].x.shape[1])
+                    tr.append((nat.addr(views[i]["ct"]), nat.addr(views[i]["codes"]), n, nrow, pitch[i], n, 1))
+                    if it + 1 < self.n_iter:
+                        tr.append((nat.addr(views[i]["wt"]), nat.addr(views[i]["wcur"]), n, nrow, pitch[i], n, 4))
+                transpose(tr, "transpose sweep outputs")
             rp = []
             for i in ef_idx:
                 j = jobs[i]
