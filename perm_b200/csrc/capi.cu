@@ -472,9 +472,10 @@ int cp_transpose_batch(const cp_transpose_job* jobs, int count, void* stream) {
       d.cols = j.cols;
       d.src_ld = j.src_ld;
       d.dst_ld = j.dst_ld;
-      d.tiles_c = (j.cols + 31) / 32;
+      const int T = cpk::transpose_tile_dim(eb);
+      d.tiles_c = (j.cols + T - 1) / T;
       d.tile0 = tiles;
-      tiles += cpk::transpose_tiles(j.rows, j.cols);
+      tiles += cpk::transpose_tiles(j.rows, j.cols, eb);
     }
   }
   return CP_OK;

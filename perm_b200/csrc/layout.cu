@@ -2,8 +2,8 @@
 // one lane per row, so it wants its per-element arrays (weights, codes, compensated weights)
 // column-major: a warp's access to one column of 32 rows is then one contiguous segment
 // instead of 32 row-strided sectors.  These kernels move tensors between the row-major
-// storage order and that layout with 32 x 32 tiles staged in shared memory, so both the reads
-// and the writes are coalesced.
+// storage order and that layout with tiles staged in shared memory (64 x 64 floats, 128 x 128
+// bytes), so both the reads and the writes are coalesced.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "layout_kernels.h"
@@ -11,43 +11,96 @@
 
 namespace cpk {
 
-// dst[c * dst_ld + r] = src[r * src_ld + c] over one 32 x 32 tile per CTA (256 threads).
-template <typename E>
-__global__ void __launch_bounds__(256) transpose_batch_kernel(const __grid_constant__ TrBatch b) {
-  __shared__ E tile[32][33];
+__device__ __forceinline__ const TrDesc& tr_desc(const TrBatch& b, int64_t cta) {
   int lo = 0, hi = b.count - 1;
-  const int64_t cta = blockIdx.x;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (b.d[mid].tile0 <= cta) lo = mid;
     else hi = mid - 1;
   }
-  const TrDesc& t = b.d[lo];
+  return b.d[lo];
+}
+
+// float32: dst[c * dst_ld + r] = src[r * src_ld + c] over one 64 x 64 tile per CTA (256
+// threads, 16 elements each); warps read and write 128-byte row segments.
+__global__ void __launch_bounds__(256) transpose_f32_kernel(const __grid_constant__ TrBatch b) {
+  __shared__ float tile[64][65];
+  const int64_t cta = blockIdx.x;
+  const TrDesc& t = tr_desc(b, cta);
   const int64_t k = cta - t.tile0;
-  const int64_t r0 = (k / t.tiles_c) * 32, c0 = (k % t.tiles_c) * 32;
-  const E* __restrict__ src = static_cast<const E*>(t.src);
-  E* __restrict__ dst = static_cast<E*>(t.dst);
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r0 = (k / t.tiles_c) * 64, c0 = (k % t.tiles_c) * 64;
+  const float* __restrict__ src = static_cast<const float*>(t.src);
+  float* __restrict__ dst = static_cast<float*>(t.dst);
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  float v[16];
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int64_t r = r0 + ty + 8 * i, c = c0 + tx;
-    if (r < t.rows && c < t.cols) tile[ty + 8 * i][tx] = src[r * t.src_ld + c];
+  for (int i = 0; i < 16; i++) {
+    const int64_t r = r0 + ty + 4 * i, c = c0 + tx;
+    v[i] = (r < t.rows && c < t.cols) ? src[r * t.src_ld + c] : 0.0f;
   }
+#pragma unroll
+  for (int i = 0; i < 16; i++) tile[ty + 4 * i][tx] = v[i];
   __syncthreads();
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int64_t c = c0 + ty + 8 * i, r = r0 + tx;
-    if (r < t.rows && c < t.cols) dst[c * t.dst_ld + r] = tile[tx][ty + 8 * i];
+  for (int i = 0; i < 16; i++) {
+    const int64_t c = c0 + ty + 4 * i, r = r0 + tx;
+    if (r < t.rows && c < t.cols) dst[c * t.dst_ld + r] = tile[tx][ty + 4 * i];
   }
 }
 
-int64_t transpose_tiles(int64_t rows, int64_t cols) { return ((rows + 31) / 32) * ((cols + 31) / 32); }
+// bytes: one 128 x 128 tile per CTA; full tiles move 4-byte words both ways (a warp reads or
+// writes one 128-byte row segment), edge tiles go byte by byte.
+__global__ void __launch_bounds__(256) transpose_u8_kernel(const __grid_constant__ TrBatch b) {
+  __shared__ uint8_t tile[128][132];
+  const int64_t cta = blockIdx.x;
+  const TrDesc& t = tr_desc(b, cta);
+  const int64_t k = cta - t.tile0;
+  const int64_t r0 = (k / t.tiles_c) * 128, c0 = (k % t.tiles_c) * 128;
+  const uint8_t* __restrict__ src = static_cast<const uint8_t*>(t.src);
+  uint8_t* __restrict__ dst = static_cast<uint8_t*>(t.dst);
+  const int tid = threadIdx.x;
+  const bool full = r0 + 128 <= t.rows && c0 + 128 <= t.cols && ((t.src_ld | t.dst_ld) & 3) == 0 &&
+                    ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 3) == 0;
+  if (full) {
+#pragma unroll 4
+    for (int w = tid; w < 128 * 32; w += 256) {
+      const int r = w >> 5, wc = w & 31;
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(src + (r0 + r) * t.src_ld + c0 + 4 * wc);
+      *reinterpret_cast<uint32_t*>(&tile[r][4 * wc]) = v;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int w = tid; w < 128 * 32; w += 256) {
+      const int c = w >> 5, wr = w & 31;
+      const uint32_t v = (uint32_t)tile[4 * wr][c] | ((uint32_t)tile[4 * wr + 1][c] << 8) |
+                         ((uint32_t)tile[4 * wr + 2][c] << 16) | ((uint32_t)tile[4 * wr + 3][c] << 24);
+      *reinterpret_cast<uint32_t*>(dst + (c0 + c) * t.dst_ld + r0 + 4 * wr) = v;
+    }
+  } else {
+    for (int e = tid; e < 128 * 128; e += 256) {
+      const int r = e >> 7, c = e & 127;
+      if (r0 + r < t.rows && c0 + c < t.cols) tile[r][c] = src[(r0 + r) * t.src_ld + c0 + c];
+    }
+    __syncthreads();
+    for (int e = tid; e < 128 * 128; e += 256) {
+      const int c = e >> 7, r = e & 127;
+      if (r0 + r < t.rows && c0 + c < t.cols) dst[(c0 + c) * t.dst_ld + r0 + r] = tile[r][c];
+    }
+  }
+}
+
+int transpose_tile_dim(int elem_bytes) { return elem_bytes == 1 ? 128 : 64; }
+
+int64_t transpose_tiles(int64_t rows, int64_t cols, int elem_bytes) {
+  const int T = transpose_tile_dim(elem_bytes);
+  return ((rows + T - 1) / T) * ((cols + T - 1) / T);
+}
 
 int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles, cudaStream_t stream) {
   if (b.count == 0 || total_tiles == 0) return 0;
   if (total_tiles > INT32_MAX) return 2;
-  if (elem_bytes == 4) transpose_batch_kernel<float><<<(unsigned)total_tiles, 256, 0, stream>>>(b);
-  else if (elem_bytes == 1) transpose_batch_kernel<uint8_t><<<(unsigned)total_tiles, 256, 0, stream>>>(b);
+  if (elem_bytes == 4) transpose_f32_kernel<<<(unsigned)total_tiles, 256, 0, stream>>>(b);
+  else if (elem_bytes == 1) transpose_u8_kernel<<<(unsigned)total_tiles, 256, 0, stream>>>(b);
   else return 2;
   note_launch();
   return 0;

@@ -5,7 +5,8 @@
 
 namespace cpk {
 // One transpose of a grouped launch: dst[c * dst_ld + r] = src[r * src_ld + c], CTAs
-// [tile0, tile0 + transpose_tiles(rows, cols)) over 32 x 32 tiles (tiles_c tiles per row).
+// [tile0, tile0 + transpose_tiles(rows, cols, elem_bytes)) over square tiles of
+// transpose_tile_dim(elem_bytes) (tiles_c tiles per row of tiles).
 struct TrDesc {
   const void* src;
   void* dst;
@@ -16,6 +17,7 @@ struct TrBatch {
   int count;
   TrDesc d[kTrBatchMax];
 };
-int64_t transpose_tiles(int64_t rows, int64_t cols);
+int transpose_tile_dim(int elem_bytes);
+int64_t transpose_tiles(int64_t rows, int64_t cols, int elem_bytes);
 int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles, cudaStream_t stream);
 }  // namespace cpk
