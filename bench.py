@@ -215,13 +215,22 @@ class Workload:
             self.diags[k] = torch.diagonal(H).cpu().numpy()
         self.ef_keys = sorted({self.spec_by_name[u.name].hkey for u in self.units
                                if self.spec_by_name[u.name].mode == "EF"})
+        # the rank's weights are views into one flat float32 buffer (e2e moves them with one
+        # copy and one conversion)
+        total = sum((u.r1 - u.r0) * self.spec_by_name[u.name].n for u in self.units)
+        self.x_flat = torch.empty(max(1, total), dtype=torch.float32, device="cuda")
         self.x = {}
         full_cache = {}
+        off = 0
         for u in self.units:
             sp = self.spec_by_name[u.name]
             if sp.name not in full_cache:
                 full_cache = {sp.name: model.synth_weights(torch, sp, args.seed, "cuda")}
-            self.x[self.uid(u)] = full_cache[sp.name][u.r0:u.r1].contiguous()
+            cnt = (u.r1 - u.r0) * sp.n
+            v = self.x_flat[off:off + cnt].view(u.r1 - u.r0, sp.n)
+            v.copy_(full_cache[sp.name][u.r0:u.r1])
+            self.x[self.uid(u)] = v
+            off += cnt
         del full_cache
         self.qw = {k: torch.from_numpy(self.diags[k].astype(np.float32)).cuda() for k in self.diags}
 
@@ -419,53 +428,78 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
     pinned memory every step, packed bytes copied back to pinned memory."""
     from perm_b200 import _native as nat
     from perm_b200.shard import gather_to_rank0
-    host_w, dev_w16 = {}, {}
-    for j in jobs:
-        w16 = j.x.to(torch.float16)
-        host_w[j.name] = w16.cpu().pin_memory()
-        dev_w16[j.name] = torch.empty_like(w16)
-    host_h, dev_h = {}, {}
-    for k in wl.ef_keys + [k for k in wl.hess if k not in wl.ef_keys]:
-        H = wl.hess[k].float()
-        amax = float(H.abs().max())
-        hscale = amax / 32768.0 if amax > 32768.0 else 1.0
-        h16 = (H / hscale).to(torch.float16)
-        host_h[k] = (h16.cpu().pin_memory(), torch.diagonal(H).contiguous().cpu().pin_memory(), hscale)
-        dev_h[k] = (torch.empty_like(h16), torch.empty(H.shape[0], dtype=torch.float32, device="cuda"),
-                    torch.empty_like(wl.hess[k]))
+    # weights: one pinned float16 image of the rank's flat float32 buffer
+    host_w = wl.x_flat.to(torch.float16).cpu().pin_memory()
+    dev_w16 = torch.empty_like(host_w, device="cuda")
+    # Hessians in stored form, one pinned float16 image per size, diagonals in one buffer
+    keys = wl.ef_keys + [k for k in wl.hess if k not in wl.ef_keys]
+    by_size = {}
+    for k in keys:
+        by_size.setdefault(int(wl.hess[k].shape[0]), []).append(k)
+    host_h16, dev_h16, hscale, h_off = {}, {}, {}, {}
+    diag_parts, d_off, dn = [], {}, 0
+    for n, ks in by_size.items():
+        parts, off = [], 0
+        for k in ks:
+            H = wl.hess[k].float()
+            amax = float(H.abs().max())
+            hscale[k] = amax / 32768.0 if amax > 32768.0 else 1.0
+            parts.append((H / hscale[k]).to(torch.float16).reshape(-1))
+            h_off[k] = off
+            off += n * n
+            diag_parts.append(torch.diagonal(H).contiguous())
+            d_off[k] = dn
+            dn += n
+        host_h16[n] = torch.cat(parts).cpu().pin_memory()
+        dev_h16[n] = torch.empty_like(host_h16[n], device="cuda")
+    host_d32 = torch.cat(diag_parts).cpu().pin_memory()
+    dev_d32 = torch.empty_like(host_d32, device="cuda")
+    dev_H = {k: torch.empty_like(wl.hess[k]) for k in keys}
     host_out = torch.empty(max(1, my_bytes if world == 1 else (sum(all_sizes) if rank == 0 else 0)),
                            dtype=torch.uint8).pin_memory()
-    h2d = sum(v.numel() * 2 for v in host_w.values()) + sum(v[0].numel() * 2 + v[1].numel() * 4
-                                                          for v in host_h.values())
+    h2d = host_w.numel() * 2 + sum(v.numel() * 2 for v in host_h16.values()) + host_d32.numel() * 4
     d2h = sum(all_sizes) if rank == 0 else 0
-    s = nat.stream_ptr(torch)
     copy_stream = torch.cuda.Stream()
+    hcopy_stream = torch.cuda.Stream(priority=-1)   # its decodes must not queue behind the fits
+    hs_ = nat.stream_ptr(torch, hcopy_stream)
     # the stored diagonal is exact float32 and the decoded H carries it unchanged, so the
     # host copy gives act order and damping without reading H back
-    host_diag = {k: v[1].numpy().astype(np.float64) for k, v in host_h.items()}
+    hd = host_d32.numpy().astype(np.float64)
+    host_diag = {k: hd[d_off[k]:d_off[k] + int(wl.hess[k].shape[0])] for k in keys}
 
     def step():
-        # Hessians first (the factorisations need only them), the weights on a copy stream
-        # that runs beside the factorisations; the fits wait for the weights
-        for k, (h16, d32, hscale) in host_h.items():
-            dh16, dd32, H = dev_h[k]
-            dh16.copy_(h16, non_blocking=True)
-            dd32.copy_(d32, non_blocking=True)
-            nat.check(nat.lib().cp_hessian_decode(nat.ptr(dh16), nat.ptr(dd32), float(hscale), H.shape[0],
-                                                  nat.ptr(H), s), "hessian_decode")
-        hs = {k: dev_h[k][2] for k in wl.ef_keys}
-        for j in jobs:
-            if j.qw is not None:
-                j.qw.copy_(dev_h[j.hkey][1])
-        copy_stream.wait_stream(torch.cuda.current_stream())
+        # PCIe order: all diagonals (the fits' imatrix), the Hessians largest size first
+        # (each size's factor chain starts as soon as its Hessians are decoded), then the
+        # weights, which only the fits wait for.
+        sizes = sorted(by_size, reverse=True)
+        ready = {}
+
+        def hessians(ns):
+            with torch.cuda.stream(hcopy_stream):
+                for n in ns:
+                    dev_h16[n].copy_(host_h16[n], non_blocking=True)
+                    for k in by_size[n]:
+                        nat.check(nat.lib().cp_hessian_decode(
+                            dev_h16[n].data_ptr() + 2 * h_off[k], dev_d32.data_ptr() + 4 * d_off[k],
+                            float(hscale[k]), n, nat.ptr(dev_H[k]), hs_), "hessian_decode")
+                    ready[n] = torch.cuda.Event()
+                    ready[n].record(hcopy_stream)
+
+        hcopy_stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(hcopy_stream):
+            dev_d32.copy_(host_d32, non_blocking=True)
+            for k in wl.qw:
+                wl.qw[k].copy_(dev_d32[d_off[k]:d_off[k] + wl.qw[k].numel()])
+        hessians(sizes)
+        copy_stream.wait_stream(hcopy_stream)
         with torch.cuda.stream(copy_stream):
-            for j in jobs:
-                dev_w16[j.name].copy_(host_w[j.name], non_blocking=True)
-                j.x.copy_(dev_w16[j.name])
+            dev_w16.copy_(host_w, non_blocking=True)
+            wl.x_flat.copy_(dev_w16)
             weights_ready = torch.cuda.Event()
             weights_ready.record(copy_stream)
+        hs = {k: dev_H[k] for k in wl.ef_keys}
         enc.run(jobs, hs, {k: host_diag[k] for k in wl.ef_keys}, stats=True, outputs=outputs,
-                inputs_event=weights_ready)
+                inputs_event=weights_ready, ready_events=ready)
         if world > 1:
             bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
             if rank == 0:

@@ -72,12 +72,14 @@ class Encoder:
         self._fstreams = None
 
     # ---------------------------------------------------------------- factorisation
-    def factor(self, hessians, diags=None, _max_tries=6, check=True):
+    def factor(self, hessians, diags=None, _max_tries=6, check=True, ready_events=None):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
         Returns {key: Factor}.  All first attempts go out as one batched call (same-size
         Hessians advance through each factorisation step in a single launch); the status
         words are read with one synchronisation and only a non-positive pivot triggers the
-        reference's damp escalation for that Hessian."""
+        reference's damp escalation for that Hessian.  ready_events: {n: CUDA event} after
+        which the Hessians of size n are on the device (each size's chain waits for its own
+        event instead of for everything queued on this stream)."""
         torch = self.torch
         L = nat.lib()
         keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
@@ -107,7 +109,7 @@ class Encoder:
         for gi, n in enumerate(sizes):
             grp = groups[n]
             st = self._fstreams[gi]
-            st.wait_event(ready)
+            st.wait_event(ready_events[n] if ready_events is not None and n in ready_events else ready)
             sp = nat.stream_ptr(torch, st)
             oh = self._forder_host[n]
             ohn = oh.numpy()
@@ -160,14 +162,15 @@ class Encoder:
             redone.append(k)
         return redone
 
-    def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None):
+    def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None, ready_events=None):
         """factor() + encode() with the factorisations overlapped with the round-1 fits: the
         factor chains start on side streams, the fits (which need no U) go first on this
         stream, and the status words are read once at the end; tensors whose Hessian needed
         damp escalation are encoded again with the escalated factor.  inputs_event: a CUDA
         event after which the weights are ready (e.g. copies on another stream); the
-        factorisations, which need only the Hessians, do not wait for it."""
-        factors = self.factor(hessians, diags, check=False)
+        factorisations, which need only the Hessians, do not wait for it.  ready_events: as
+        in factor()."""
+        factors = self.factor(hessians, diags, check=False, ready_events=ready_events)
         if inputs_event is not None:
             (self.stream if self.stream is not None else self.torch.cuda.current_stream()).wait_event(inputs_event)
         raws, st = self.encode(jobs, factors, stats=stats, outputs=outputs, factor_event=self._factor_done)
