@@ -118,42 +118,64 @@ __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, b
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
 }
 
-// 64 x 64 FP64 tile product on CUDA cores: acc = sum_l A[i][l] * Bop[l][j] over l < k_len.
-// 64 threads, each an 8 x 8 register tile (rows tm + 8r, columns tn + 8c); K streamed in chunks
-// of 16 through a two-stage cp.async pipeline (rows padded to 18 doubles: conflict-free).
+// 64 x 64 FP64 tile product on the FP64 tensor path: acc = sum_l A[i][l] * Bop[l][j] over
+// l < k_len, with mma.sync m16n8k16 (f64).  kFT = 128 threads: warp w owns the 32 x 32
+// quarter (rows 32 (w >> 1), columns 32 (w & 1)) as 2 x 4 fragments; with g = lane >> 2 and
+// q = lane & 3, acc[mf][nf][v] is element
+//   row 32 (w >> 1) + 16 mf + g + 8 (v >> 1),  column 32 (w & 1) + 8 nf + 2 q + (v & 1)
+// (tile_for_each).  K streams in chunks of 16 through a two-stage zero-filling cp.async
+// pipeline.  Shared-memory pitches (20 doubles for rows of A and of B stored [N][K], 68 for
+// B stored [K][N]) keep the fragment loads free of bank conflicts.
 // B_NK: B is stored [N][K] (Bop = B^T, the A*B^T form); otherwise B is [K][N].
 // Rows >= m_lim of A and columns >= n_lim of Bop read as zero.
+constexpr int kFT = 128;
+constexpr int kAP = 20;
+constexpr int kBP = 68;
+
+__device__ __forceinline__ void mma_f64(double (&d)[4], const double (&a)[8], const double (&b)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f64.f64.f64.f64 {%0, %1, %2, %3}, {%4, %5, %6, %7, %8, %9, %10, %11}, "
+      "{%12, %13, %14, %15}, {%0, %1, %2, %3};"
+      : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+      : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]), "d"(b[0]),
+        "d"(b[1]), "d"(b[2]), "d"(b[3]));
+}
+
 template <bool B_NK>
 __device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, const double* __restrict__ B, int ldb,
-                                       int m_lim, int n_lim, int k_len, double (&acc)[8][8]) {
-  __shared__ __align__(16) double sa[2][64][18];
-  __shared__ __align__(16) double sb[2][64][18];   // [N][K] chunk (B_NK) or [K][N] packed as [16][66] below
-  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
+                                       int m_lim, int n_lim, int k_len, double (&acc)[2][4][4]) {
+  __shared__ __align__(16) double sa[2][64 * kAP];
+  __shared__ __align__(16) double sb[2][B_NK ? 64 * kAP : 16 * kBP];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, g = lane >> 2, q = lane & 3;
+  const int wm = 32 * (warp >> 1), wn = 32 * (warp & 1);
 #pragma unroll
-  for (int i = 0; i < 8; i++)
+  for (int i = 0; i < 2; i++)
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) acc[i][j][v] = 0.0;
   auto load = [&](int l0, int buf) {
 #pragma unroll
-    for (int q = 0; q < 8; q++) {  // A chunk: 64 rows x 16 doubles = 512 x 16 bytes
-      const int i = t + 64 * q, r = i >> 3, kk = (i & 7) * 2;
+    for (int k = 0; k < 512 / kFT; k++) {  // A chunk: 64 rows x 16 doubles = 512 x 16 bytes
+      const int i = t + kFT * k, r = i >> 3, kk = (i & 7) * 2;
       const bool ok = r < m_lim && l0 + kk < k_len;
-      cp_async16_zfill(&sa[buf][r][kk], ok ? (const void*)(A + (size_t)r * lda + l0 + kk) : (const void*)A, ok);
+      cp_async16_zfill(&sa[buf][r * kAP + kk], ok ? (const void*)(A + (size_t)r * lda + l0 + kk) : (const void*)A, ok);
     }
     if (B_NK) {
 #pragma unroll
-      for (int q = 0; q < 8; q++) {
-        const int i = t + 64 * q, c = i >> 3, kk = (i & 7) * 2;
+      for (int k = 0; k < 512 / kFT; k++) {
+        const int i = t + kFT * k, c = i >> 3, kk = (i & 7) * 2;
         const bool ok = c < n_lim && l0 + kk < k_len;
-        cp_async16_zfill(&sb[buf][c][kk], ok ? (const void*)(B + (size_t)c * ldb + l0 + kk) : (const void*)B, ok);
+        cp_async16_zfill(&sb[buf][c * kAP + kk], ok ? (const void*)(B + (size_t)c * ldb + l0 + kk) : (const void*)B,
+                         ok);
       }
     } else {
-      double* sbk = &sb[buf][0][0];  // viewed as [16][72]: row kk holds Bop[kk][0..63]
 #pragma unroll
-      for (int q = 0; q < 8; q++) {
-        const int i = t + 64 * q, kk = i >> 5, c = (i & 31) * 2;
+      for (int k = 0; k < 512 / kFT; k++) {  // row kk of the chunk holds Bop[kk][0..63]
+        const int i = t + kFT * k, kk = i >> 5, c = (i & 31) * 2;
         const bool ok = c < n_lim && l0 + kk < k_len;
-        cp_async16_zfill(sbk + kk * 72 + c, ok ? (const void*)(B + (size_t)(l0 + kk) * ldb + c) : (const void*)B, ok);
+        cp_async16_zfill(&sb[buf][kk * kBP + c], ok ? (const void*)(B + (size_t)(l0 + kk) * ldb + c) : (const void*)B,
+                         ok);
       }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
@@ -169,50 +191,60 @@ __device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, co
       asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     }
     __syncthreads();
-    const double* sbk = &sb[buf][0][0];
+    double a[2][8], bf[4][4];
 #pragma unroll
-    for (int kk = 0; kk < 16; kk++) {
-      double av[8], bv[8];
+    for (int mf = 0; mf < 2; mf++)
 #pragma unroll
-      for (int r = 0; r < 8; r++) av[r] = sa[buf][tm + 8 * r][kk];
+      for (int r = 0; r < 8; r++) a[mf][r] = sa[buf][(wm + 16 * mf + g + 8 * (r & 1)) * kAP + q + 4 * (r >> 1)];
 #pragma unroll
-      for (int c = 0; c < 8; c++) bv[c] = B_NK ? sb[buf][tn + 8 * c][kk] : sbk[kk * 72 + tn + 8 * c];
+    for (int nf = 0; nf < 4; nf++)
 #pragma unroll
-      for (int r = 0; r < 8; r++)
+      for (int v = 0; v < 4; v++)
+        bf[nf][v] = B_NK ? sb[buf][(wn + 8 * nf + g) * kAP + q + 4 * v] : sb[buf][(q + 4 * v) * kBP + wn + 8 * nf + g];
 #pragma unroll
-        for (int c = 0; c < 8; c++) acc[r][c] = fma(av[r], bv[c], acc[r][c]);
-    }
+    for (int mf = 0; mf < 2; mf++)
+#pragma unroll
+      for (int nf = 0; nf < 4; nf++) mma_f64(acc[mf][nf], a[mf], bf[nf]);
     __syncthreads();
   }
+}
+
+// Calls f(row, column, value) for every element of the 64 x 64 tile this thread holds.
+template <typename F>
+__device__ __forceinline__ void tile_for_each(const double (&acc)[2][4][4], F f) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int mf = 0; mf < 2; mf++)
+#pragma unroll
+    for (int nf = 0; nf < 4; nf++)
+#pragma unroll
+      for (int v = 0; v < 4; v++)
+        f(32 * (warp >> 1) + 16 * mf + g + 8 * (v >> 1), 32 * (warp & 1) + 8 * nf + 2 * q + (v & 1), acc[mf][nf][v]);
 }
 
 // Left-looking Cholesky step j, before the diagonal factorisation:
 //   A[j:n, j:j+64] -= L[j:n, 0:j] * L[j:j+64, 0:j]^T        (one 64-row tile per CTA)
 // With S > 1 the K range is split over blockIdx.y and each CTA writes its partial product;
 // chol_reduce_kernel then subtracts the partials from the block column in order.
-__global__ void __launch_bounds__(64) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+__global__ void __launch_bounds__(kFT) chol_update_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.z];
   if (*fb.status[blockIdx.z]) return;
   const int r0 = j + blockIdx.x * 64;
   const int q = blockIdx.y, chunk = kchunk(j, S);
   const int k0 = q * chunk, k1 = min(j, k0 + chunk);
-  double acc[8][8];
+  double acc[2][4][4];
   tile64<true>(A + (size_t)r0 * n + k0, n, A + (size_t)j * n + k0, n, n - r0, 64, k1 - k0, acc);
-  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
   double* part = part_base(A, n) + (size_t)q * n * NB;
-#pragma unroll
-  for (int r = 0; r < 8; r++)
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const int rr = r0 + tm + 8 * r, cc = tn + 8 * c;
-      if (rr >= n) continue;
-      if (S == 1) {
-        if (rr >= j + cc) A[(size_t)rr * n + j + cc] -= acc[r][c];
-      } else {
-        part[(size_t)rr * NB + cc] = acc[r][c];
-      }
+  tile_for_each(acc, [&](int r, int c, double v) {
+    const int rr = r0 + r;
+    if (rr >= n) return;
+    if (S == 1) {
+      if (rr >= j + c) A[(size_t)rr * n + j + c] -= v;
+    } else {
+      part[(size_t)rr * NB + c] = v;
     }
+  });
 }
 
 // Split-K reduction of a Cholesky step's update: A[r][j+c] -= part_0 - ... - part_{S-1}, in
@@ -253,29 +285,25 @@ __global__ void __launch_bounds__(256) trinv_reduce_kernel(const __grid_constant
 }
 
 // Panel below the diagonal block: A[j+64:n, j:j+64] := A * inv(L_jj)^T (inverse on the diagonal).
-__global__ void __launch_bounds__(64) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
+__global__ void __launch_bounds__(kFT) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
   if (*fb.status[blockIdx.y]) return;
   const int r0 = j + 64 + blockIdx.x * 64;
-  double acc[8][8];
+  double acc[2][4][4];
   tile64<true>(A + (size_t)r0 * n + j, n, A + (size_t)j * n + j, n, n - r0, 64, 64, acc);
   __syncthreads();  // every CTA reads only its own rows of the panel, so in-place is safe
-  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
-#pragma unroll
-  for (int r = 0; r < 8; r++)
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const int rr = r0 + tm + 8 * r;
-      if (rr < n) A[(size_t)rr * n + j + tn + 8 * c] = acc[r][c];
-    }
+  tile_for_each(acc, [&](int r, int c, double v) {
+    const int rr = r0 + r;
+    if (rr < n) A[(size_t)rr * n + j + c] = v;
+  });
 }
 
 // Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
 //   T = -Linv22 * L21          (rows below, into scratch; Linv22 is lower triangular)
 // With S > 1 the K range is split over blockIdx.y; partial products go to the partial-tile
 // scratch and trinv_reduce_kernel forms T from them in order.
-__global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+__global__ void __launch_bounds__(kFT) trmm_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
   const int n = fb.n;
   double* __restrict__ Pw = fb.P[blockIdx.z];
   const double* __restrict__ A = Pw;
@@ -287,23 +315,18 @@ __global__ void __launch_bounds__(64) trmm_kernel(const __grid_constant__ Factor
   const int k_len = r0 + m - base;  // rows r0.. of Linv22 vanish right of column r0+m-1
   const int q = blockIdx.y, chunk = kchunk(n - base, S);
   const int k0 = q * chunk, k1 = min(k_len, k0 + chunk);
-  double acc[8][8];
+  double acc[2][4][4];
   tile64<false>(A + (size_t)r0 * n + base + k0, n, A + (size_t)(base + k0) * n + j, n, m, 64, k1 - k0, acc);
-  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
   double* part = part_base(Pw, n) + (size_t)q * n * NB;
-#pragma unroll
-  for (int r = 0; r < 8; r++)
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const int rr = tm + 8 * r;
-      if (rr >= m) continue;
-      if (S == 1) T[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = -acc[r][c];
-      else part[(size_t)(r0 - base + rr) * NB + tn + 8 * c] = acc[r][c];
-    }
+  tile_for_each(acc, [&](int r, int c, double v) {
+    if (r >= m) return;
+    if (S == 1) T[(size_t)(r0 - base + r) * NB + c] = -v;
+    else part[(size_t)(r0 - base + r) * NB + c] = v;
+  });
 }
 
 //   L21 := T * inv(L_jj)   (inv(L_jj) already sits on the diagonal)
-__global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
+__global__ void __launch_bounds__(kFT) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.y];
   double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
@@ -311,16 +334,11 @@ __global__ void __launch_bounds__(64) trinv_apply_kernel(const __grid_constant__
   const int base = j + NB;
   const int r0 = base + blockIdx.x * 64;
   const int m = min(64, n - r0);
-  double acc[8][8];
+  double acc[2][4][4];
   tile64<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, 64, 64, acc);
-  const int t = threadIdx.x, tm = t >> 3, tn = t & 7;
-#pragma unroll
-  for (int r = 0; r < 8; r++)
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const int rr = tm + 8 * r;
-      if (rr < m) A[(size_t)(r0 + rr) * n + j + tn + 8 * c] = acc[r][c];
-    }
+  tile_for_each(acc, [&](int r, int c, double v) {
+    if (r < m) A[(size_t)(r0 + r) * n + j + c] = v;
+  });
 }
 
 // U[i][j] = Linv[n-1-i][n-1-j] for j >= i, else 0 (cast to OutT).
@@ -352,7 +370,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   for (int j = 0; j < n; j += NB) {
     const int S = j > 0 ? ksplit(j) : 1;
     if (j > 0) {
-      chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
+      chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)S, (unsigned)cnt), kFT, 0, stream>>>(fb, j, S);
       note_launch();
       if (S > 1) {
         chol_reduce_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)cnt), 256, 0, stream>>>(fb, j, S);
@@ -362,7 +380,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j);
     note_launch();
     if (n - j - NB > 0) {
-      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), 64, 0, stream>>>(fb, j);
+      trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), kFT, 0, stream>>>(fb, j);
       note_launch();
     }
   }
@@ -371,13 +389,13 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   for (int j = n - 2 * NB; j >= 0; j -= NB) {
     const unsigned tiles = (unsigned)((n - j - NB + 63) / 64);
     const int S = ksplit(n - j - NB);
-    trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), 64, 0, stream>>>(fb, j, S);
+    trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), kFT, 0, stream>>>(fb, j, S);
     note_launch();
     if (S > 1) {
       trinv_reduce_kernel<<<dim3(tiles, (unsigned)cnt), 256, 0, stream>>>(fb, j, S);
       note_launch();
     }
-    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), 64, 0, stream>>>(fb, j);
+    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), kFT, 0, stream>>>(fb, j);
     note_launch();
   }
   {
