@@ -78,4 +78,68 @@ __device__ __forceinline__ float np_sum(const float (&a)[N]) {
 __device__ __forceinline__ uint16_t f16bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
 __device__ __forceinline__ float f16tof32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// ---------------------------------------------------------------- packed float32 pairs
+// Two float32 values in one 64-bit register pair (the even element in the low half), operated
+// on by the sm_100 f32x2 instructions: one issue slot for two results.  Sums and differences
+// are add/sub.rn.f32x2.  Products are fma.rn.f32x2 with a -0.0 addend that arrives at run
+// time (a kernel argument): fl(a * b + -0) == fl(a * b) for every input, signed zeros
+// included, and ptxas cannot fuse such a product with a following add, as it may a packed
+// multiply.  Each pair operation therefore rounds exactly like the scalar float32 operation
+// (and numpy's elementwise ufunc) it stands for.
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(f32x2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// fl(a * b) per half; nz2 holds -0.0 in both halves.
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b, f32x2 nz2) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(nz2));
+  return r;
+}
+// nint_clip_f on both halves: the magic add and subtract as pair operations, the clamp on
+// the bit patterns of each half.
+__device__ __forceinline__ f32x2 nint_clip2(f32x2 v, int lo, int hi, f32x2 magic2) {
+  float a, b;
+  upk2(add2(v, magic2), a, b);
+  int ia = (__float_as_int(a) & 0x007FFFFF) | 0x4B000000;
+  int ib = (__float_as_int(b) & 0x007FFFFF) | 0x4B000000;
+  ia = min(max(ia, 0x4B400000 + lo), 0x4B400000 + hi);
+  ib = min(max(ib, 0x4B400000 + lo), 0x4B400000 + hi);
+  return sub2(pk2(__int_as_float(ia), __int_as_float(ib)), magic2);
+}
+
+// Pw8 over pairs: pair k carries elements 2k and 2k + 1, which land in accumulators
+// 2(k & 3) and 2(k & 3) + 1, so accumulator pair k & 3 receives them in the scalar order.
+struct Pw8x2 {
+  f32x2 r[4];
+  __device__ __forceinline__ void addk(int k, f32x2 v) {  // k a compile-time constant after unrolling
+    if (k < 4) r[k] = v; else r[k & 3] = add2(r[k & 3], v);
+  }
+  __device__ __forceinline__ float total() const {
+    float a0, a1, a2, a3, a4, a5, a6, a7;
+    upk2(r[0], a0, a1);
+    upk2(r[1], a2, a3);
+    upk2(r[2], a4, a5);
+    upk2(r[3], a6, a7);
+    const float res = ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
+    return 0.0f + res;
+  }
+};
+
 }  // namespace cpk

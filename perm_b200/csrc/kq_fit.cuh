@@ -11,10 +11,12 @@ namespace cpk {
 // Instead of copying the candidate codes on acceptance, the (iscale, min) pair that produced
 // them is recorded and the codes are recomputed once at the end (same arithmetic).
 // Outputs: scale, -min and the codes as floats (0..nmax).
+// The squared-error variant (MAD false) runs its candidate loop on packed pairs (f32x2, with
+// nz = -0.0 from a kernel argument) and keeps x - min in registers between acceptances.
 template <int N, bool MAD, bool QKX3>
 __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N], int nmax, float rmin,
                                         float rdelta, int nstep, float& o_scale, float& o_negmin,
-                                        float (&Lf)[N]) {
+                                        float (&Lf)[N], float nz = 0.0f) {
   float mn = x[0], mx = x[0];
 #pragma unroll
   for (int i = 1; i < N; i++) {
@@ -51,6 +53,69 @@ __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N]
   }
   float b_isc = iscale, b_mn = mn;
   bool b_fin = fin0;
+  if constexpr (!MAD) {
+    static_assert(N % 16 == 0, "pairs fill the 8 accumulators");
+    constexpr int P = N / 2;
+    const f32x2 nz2 = pk2(nz, nz), magic2 = pk2(kMagic, kMagic);
+    f32x2 xp[P], wp[P], xm[P];
+#pragma unroll
+    for (int k = 0; k < P; k++) {
+      xp[k] = pk2(x[2 * k], x[2 * k + 1]);
+      wp[k] = pk2(w[2 * k], w[2 * k + 1]);
+    }
+    {
+      const f32x2 mn2 = pk2(mn, mn);
+#pragma unroll
+      for (int k = 0; k < P; k++) xm[k] = sub2(xp[k], mn2);
+    }
+#pragma unroll 1
+    for (int step = 0; step <= nstep; step++) {
+      float span_cur = mx - mn;
+      span_cur = span_cur > 0.0f ? span_cur : 1.0f;
+      const float isc = (rmin + rdelta * (float)step + (float)nmax) / span_cur;
+      const f32x2 isc2 = pk2(isc, isc);
+      f32x2 lf[P];
+      Pw8x2 sl, sl2, sxl;
+#pragma unroll
+      for (int k = 0; k < P; k++) {
+        lf[k] = nint_clip2(mul2(isc2, xm[k], nz2), 0, nmax, magic2);
+        const f32x2 wl = mul2(wp[k], lf[k], nz2);
+        sl.addk(k, wl);
+        sl2.addk(k, mul2(wl, lf[k], nz2));
+        sxl.addk(k, mul2(wl, xp[k], nz2));
+      }
+      const float sum_l = sl.total(), sum_l2 = sl2.total(), sum_xl = sxl.total();
+      const float D = sum_w * sum_l2 - sum_l * sum_l;
+      const bool ok = D > 0.0f && isc <= 3.4028234663852886e38f;
+      if (ok && !dead) {
+        float this_scale = (sum_w * sum_xl - sum_x * sum_l) / D;
+        float this_min = (sum_l2 * sum_x - sum_l * sum_xl) / D;
+        if (this_min > 0.0f) {
+          this_min = 0.0f;
+          this_scale = sum_xl / sum_l2;
+        }
+        const f32x2 ts2 = pk2(this_scale, this_scale), tm2 = pk2(this_min, this_min);
+        Pw8x2 pc;
+#pragma unroll
+        for (int k = 0; k < P; k++) {
+          const f32x2 d = sub2(add2(mul2(ts2, lf[k], nz2), tm2), xp[k]);
+          pc.addk(k, mul2(wp[k], mul2(d, d, nz2), nz2));
+        }
+        const float cur = pc.total();
+        if (cur < best) {
+          best = cur;
+          scale = this_scale;
+          b_isc = isc;
+          b_mn = mn;
+          b_fin = true;
+          mn = this_min;
+          const f32x2 mn2 = pk2(mn, mn);
+#pragma unroll
+          for (int k = 0; k < P; k++) xm[k] = sub2(xp[k], mn2);
+        }
+      }
+    }
+  } else {
   float lf[N];
   for (int step = 0; step <= nstep; step++) {
     float span_cur = mx - mn;
@@ -94,6 +159,7 @@ __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N]
         mn = this_min;
       }
     }
+  }
   }
 #pragma unroll
   for (int i = 0; i < N; i++)

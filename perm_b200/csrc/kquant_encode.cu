@@ -98,7 +98,7 @@ __device__ __forceinline__ float sb_sumsq_8(const float* sq, int sub) {
 template <bool IMAT>
 __device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
                                                 int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
-                                                int64_t blk) {
+                                                int64_t blk, float nz) {
   constexpr int BB = 84;
   __shared__ __align__(16) float s_sq[IMAT ? 16 : 1][256];
   __shared__ __align__(16) uint8_t s_L[16][256];
@@ -130,7 +130,7 @@ __device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, con
 #pragma unroll
     for (int i = 0; i < 16; i++) w[i] = q[i] * sqrtf(sigma2 + xv[i] * xv[i]);
     const float sw = np_sum(w);
-    fit_qkx<16, false, true>(xv, w, 3, -0.9f, 0.05f, 36, scale, negmin, Lf);
+    fit_qkx<16, false, true>(xv, w, 3, -0.9f, 0.05f, 36, scale, negmin, Lf, nz);
     float vs[16], vw[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) {
@@ -202,7 +202,7 @@ __device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, con
 template <bool IMAT>
 __device__ __forceinline__ void q3k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
                                                 int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
-                                                int64_t blk) {
+                                                int64_t blk, float nz) {
   constexpr int BB = 110;
   __shared__ __align__(16) float s_sq[IMAT ? 16 : 1][256];
   __shared__ __align__(16) uint8_t s_L[16][256];
@@ -250,10 +250,10 @@ __device__ __forceinline__ void q3k_encode_body(const float* __restrict__ x, con
 #pragma unroll
     for (int j = 0; j < 16; j++) vs[j] = __shfl_sync(0xffffffffu, scale, j, 16);
     const float max_scale = select_idx(vs, argmax_abs(vs));
-    const bool nz = max_scale != 0.0f;
-    const float isc = nz ? -32.0f / max_scale : 0.0f;
-    my_Ls = nz ? clampi(nint(isc * scale), -32, 31) + 32 : 0;
-    d = nz ? 1.0f / isc : 0.0f;
+    const bool live = max_scale != 0.0f;
+    const float isc = live ? -32.0f / max_scale : 0.0f;
+    my_Ls = live ? clampi(nint(isc * scale), -32, 31) + 32 : 0;
+    d = live ? 1.0f / isc : 0.0f;
     if (!(fabsf(d) <= 3.4028234663852886e38f)) d = 0.0f;
   }
   const uint16_t d16 = f16bits(d);
@@ -306,7 +306,7 @@ __device__ __forceinline__ void q3k_encode_body(const float* __restrict__ x, con
 template <bool IMAT>
 __device__ __forceinline__ void q6k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
                                                 int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
-                                                int64_t blk) {
+                                                int64_t blk, float nz) {
   constexpr int BB = 210;
   __shared__ __align__(16) uint8_t s_L[16][256];
   __shared__ __align__(16) uint8_t s_out[16 * BB + 16];
@@ -382,7 +382,7 @@ __device__ __forceinline__ void q6k_encode_body(const float* __restrict__ x, con
 template <bool IMAT, bool Q5>
 __device__ __forceinline__ void q45k_encode_body(const float* __restrict__ x, const float* __restrict__ qw,
                                                  int64_t nsb_total, int64_t nsb_row, uint8_t* __restrict__ out,
-                                                 int64_t blk) {
+                                                 int64_t blk, float nz) {
   constexpr int BB = Q5 ? 176 : 144;
   constexpr int NMAX = Q5 ? 31 : 15;
   __shared__ __align__(16) float s_sq[IMAT ? 32 : 1][256];
@@ -413,7 +413,7 @@ __device__ __forceinline__ void q45k_encode_body(const float* __restrict__ x, co
 #pragma unroll
     for (int i = 0; i < 32; i++) w[i] = w[i] * sqrtf(sigma2 + xv[i] * xv[i]);
     const float sw = np_sum(w);
-    fit_qkx<32, false, true>(xv, w, NMAX, -0.9f, 0.05f, 36, scale, negmin, Lf);
+    fit_qkx<32, false, true>(xv, w, NMAX, -0.9f, 0.05f, 36, scale, negmin, Lf, nz);
     float vs[8], vw[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -447,7 +447,7 @@ __device__ __forceinline__ void q45k_encode_body(const float* __restrict__ x, co
     const float av_x = sqrtf(np_sum(sq) / 32.0f);
 #pragma unroll
     for (int i = 0; i < 32; i++) w[i] = av_x + fabsf(xv[i]);
-    fit_qkx<32, false, false>(xv, w, NMAX, Q5 ? -0.5f : -1.0f, 0.1f, Q5 ? 15 : 20, scale, negmin, Lf);
+    fit_qkx<32, false, false>(xv, w, NMAX, Q5 ? -0.5f : -1.0f, 0.1f, Q5 ? 15 : 20, scale, negmin, Lf, nz);
     float max_scale = __shfl_sync(0xffffffffu, scale, 0, 8);
     float max_min = __shfl_sync(0xffffffffu, negmin, 0, 8);
 #pragma unroll
@@ -611,23 +611,24 @@ template <int TYPE> constexpr int sb_per_cta() { return (TYPE == kQ4_K || TYPE =
 
 template <int TYPE, bool IMAT>
 __device__ __forceinline__ void encode_body(const float* x, const float* qw, int64_t nsb, int64_t nsb_row, uint8_t* out,
-                                            int64_t blk) {
-  if constexpr (TYPE == kQ2_K) q2k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
-  else if constexpr (TYPE == kQ3_K) q3k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
-  else if constexpr (TYPE == kQ4_K) q45k_encode_body<IMAT, false>(x, qw, nsb, nsb_row, out, blk);
-  else if constexpr (TYPE == kQ5_K) q45k_encode_body<IMAT, true>(x, qw, nsb, nsb_row, out, blk);
-  else q6k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk);
+                                            int64_t blk, float nz) {
+  if constexpr (TYPE == kQ2_K) q2k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk, nz);
+  else if constexpr (TYPE == kQ3_K) q3k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk, nz);
+  else if constexpr (TYPE == kQ4_K) q45k_encode_body<IMAT, false>(x, qw, nsb, nsb_row, out, blk, nz);
+  else if constexpr (TYPE == kQ5_K) q45k_encode_body<IMAT, true>(x, qw, nsb, nsb_row, out, blk, nz);
+  else q6k_encode_body<IMAT>(x, qw, nsb, nsb_row, out, blk, nz);
 }
 
 template <int TYPE, bool IMAT>
 __global__ void __launch_bounds__(256) encode_kernel(const float* __restrict__ x, const float* __restrict__ qw,
-                                                     int64_t nsb, int64_t nsb_row, uint8_t* __restrict__ out) {
-  encode_body<TYPE, IMAT>(x, qw, nsb, nsb_row, out, blockIdx.x);
+                                                     int64_t nsb, int64_t nsb_row, uint8_t* __restrict__ out,
+                                                     float nz) {
+  encode_body<TYPE, IMAT>(x, qw, nsb, nsb_row, out, blockIdx.x, nz);
 }
 
 // Grouped launch: every CTA finds its tensor in the descriptor table (sorted by first CTA).
 template <int TYPE, bool IMAT>
-__global__ void __launch_bounds__(256) encode_batch_kernel(const __grid_constant__ FitBatch b) {
+__global__ void __launch_bounds__(256) encode_batch_kernel(const __grid_constant__ FitBatch b, float nz) {
   int lo = 0, hi = b.count - 1;
   const int64_t cta = blockIdx.x;
   while (lo < hi) {
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(256) encode_batch_kernel(const __grid_constant
     else hi = mid - 1;
   }
   const FitDesc& t = b.d[lo];
-  encode_body<TYPE, IMAT>(t.x, t.qw, t.nsb, t.nsb_row, t.out, cta - t.cta0);
+  encode_body<TYPE, IMAT>(t.x, t.qw, t.nsb, t.nsb_row, t.out, cta - t.cta0, nz);
 }
 
 // ---------------------------------------------------------------------------- launchers
@@ -670,7 +671,7 @@ int launch_quantize(int type, const float* x, int64_t nrow, int64_t n, const flo
   const bool im = qw != nullptr;
   CPK_DISPATCH_ENC(type, im, ({
     const unsigned g = (unsigned)((total + sb_per_cta<T>() - 1) / sb_per_cta<T>());
-    encode_kernel<T, I><<<g, 256, 0, stream>>>(x, qw, total, nsb_row, out);
+    encode_kernel<T, I><<<g, 256, 0, stream>>>(x, qw, total, nsb_row, out, -0.0f);
   }));
   note_launch();
   return 0;
@@ -683,7 +684,7 @@ int64_t quantize_batch_ctas(int type, int64_t nsb) {
 
 int launch_quantize_batch(int type, bool imat, const FitBatch& b, int64_t total_ctas, cudaStream_t stream) {
   if (b.count == 0 || total_ctas == 0) return 0;
-  CPK_DISPATCH_ENC(type, imat, (encode_batch_kernel<T, I><<<(unsigned)total_ctas, 256, 0, stream>>>(b)));
+  CPK_DISPATCH_ENC(type, imat, (encode_batch_kernel<T, I><<<(unsigned)total_ctas, 256, 0, stream>>>(b, -0.0f)));
   note_launch();
   return 0;
 }
