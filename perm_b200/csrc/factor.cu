@@ -25,6 +25,23 @@ __host__ __device__ inline int ksplit(int K) {
   return s > kSplitMax ? kSplitMax : s;
 }
 __host__ __device__ inline int kchunk(int K, int S) { return ((K + S - 1) / S + 15) / 16 * 16; }
+
+// Split count of one batched launch: split K only while the tiles of all items leave the
+// GPU short of one wave (3 resident 128-thread tile CTAs per SM), then as little as fills it.
+// Every extra split costs a partial-tile write and a reduction pass.
+static int ksplit_batch(int K, int tiles, int count) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  const int smax = ksplit(K);
+  const long long base = (long long)tiles * count, slots = 3LL * sms;
+  if (smax <= 1 || base >= slots) return 1;
+  const int s = (int)((slots + base - 1) / base);
+  return s < smax ? s : smax;
+}
 // partial tiles live after P (n x n) and T (n x 64) in each item's workspace
 __device__ __forceinline__ double* part_base(double* P, int n) { return P + (size_t)n * n + (size_t)n * NB; }
 
@@ -43,72 +60,162 @@ __global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
   fb.P[b][(size_t)i * n + j] = v;
 }
 
-// Diagonal block at (k, k): Cholesky factor L11 of the (already updated) block, then its
-// inverse, written in place of the block.  Nothing after this step needs L11 itself: the
+// Diagonal block at (k, k): Cholesky factor L11 of the (already updated) 64 x 64 block, then
+// its inverse, written in place of the block.  Nothing after this step needs L11 itself: the
 // panel below is solved with inv(L11) and the diagonal blocks of L^-1 are exactly these
-// inverses.  256 threads, block in shared memory: each Cholesky column step scales the
-// column and updates the trailing triangle with four threads per row; each inverse column
-// step forms the row dot products with four threads per row and a shuffle reduction.
-// A non-positive (or NaN) pivot sets *status and leaves the rest of the factorisation idle.
+// inverses.  256 threads, blocked by 16:
+//   for each 16-column panel p: warp 0 factors the 16 x 16 diagonal block column by column
+//   (warp-synchronous; sqrt and rsqrt of the pivot side by side, no divisions) and inverts
+//   it (lane j forms column j); then all threads solve the rows below with that inverse
+//   (X = A * inv(Lpp)^T) and update the trailing triangle (A22 -= X X^T);
+//   inv(L11) block by block: X_ii = inv(L_ii), then for the block diagonals d = 1, 2, 3
+//   X_ij = -X_ii * sum_{k=j}^{i-1} L_ik X_kj (i = j + d).
+// About 30 block barriers instead of two per column.  A non-positive (or NaN) pivot sets
+// *status and leaves the rest of the factorisation idle.
+constexpr int kPotrfSmemBytes = (2 * 64 * 65 + 64) * (int)sizeof(double);
 __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_constant__ FactorBatch fb, int k) {
-  __shared__ double a[NB][NB + 1];
-  __shared__ double piv[NB];
-  const int t = threadIdx.x;
+  extern __shared__ __align__(16) double psm[];
+  double(*a)[65] = reinterpret_cast<double(*)[65]>(psm);            // the block, then L
+  double(*x)[65] = reinterpret_cast<double(*)[65]>(psm + 64 * 65);  // inv(L), lower
+  double* isq = psm + 2 * 64 * 65;                                   // 1 / L[c][c]
+  __shared__ int bad;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int n = fb.n;
   double* __restrict__ A = fb.P[blockIdx.x];
   int* status = fb.status[blockIdx.x];
   if (*status) return;
-  for (int i = t; i < NB * NB; i += 256) {
-    const int r = i / NB, c = i % NB;
-    double v = 0.0;
-    if (c <= r) {
-      v = A[(size_t)(k + r) * n + k + c];
-    }
-    a[r][c] = v;
+  if (t == 0) bad = 0;
+  for (int i = t; i < 64 * 64; i += 256) {
+    const int r = i >> 6, c = i & 63;
+    a[r][c] = (c <= r) ? A[(size_t)(k + r) * n + k + c] : 0.0;
   }
   __syncthreads();
-  for (int j = 0; j < NB; j++) {
-    const double d = a[j][j];
-    if (!(d > 0.0)) {  // uniform: every thread read the same pivot
+  for (int p = 0; p < 4; p++) {
+    const int c0 = 16 * p;
+    if (warp == 0) {
+      for (int c = 0; c < 16; c++) {
+        const double d = a[c0 + c][c0 + c];
+        if (!(d > 0.0)) {  // uniform: every lane read the same pivot
+          if (lane == 0) bad = 1;
+          break;
+        }
+        const double sq = sqrt(d), is = rsqrt(d);
+        __syncwarp();
+        if (lane > c && lane < 16) a[c0 + lane][c0 + c] *= is;
+        if (lane == 0) {
+          a[c0 + c][c0 + c] = sq;
+          isq[c0 + c] = is;
+        }
+        __syncwarp();
+        const int r = lane & 15;  // row r, columns c + 1 + (lane >> 4) + 2i up to the diagonal
+        if (r > c) {
+          const double lrc = a[c0 + r][c0 + c];
+          for (int kk = c + 1 + (lane >> 4); kk <= r; kk += 2) a[c0 + r][c0 + kk] -= lrc * a[c0 + kk][c0 + c];
+        }
+        __syncwarp();
+      }
+      __syncwarp();  // lane 0's bad flag
+      if (!bad && lane < 16) {  // inverse of the 16 x 16 factor into x's diagonal block
+        const int j = lane;
+        double col[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          double s = 0.0;
+#pragma unroll
+          for (int kk = 0; kk < i; kk++) s = fma(a[c0 + i][c0 + kk], col[kk], s);
+          col[i] = (i < j) ? 0.0 : (i == j ? isq[c0 + i] : -isq[c0 + i] * s);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[c0 + i][c0 + j] = col[i];
+      }
+    }
+    __syncthreads();
+    if (bad) {
       if (t == 0) *status = 1;
       return;
     }
-    const double sq = sqrt(d);
-    if (t == 0) piv[j] = sq;
-    const int m = NB - 1 - j;
-    if (t < m) a[j + 1 + t][j] /= sq;
+    const int m = 48 - c0;  // rows below the panel
+    if (m == 0) break;
+    {  // X = A[rows][panel] * inv(Lpp)^T, at most 3 elements a thread
+      double v[3];
+#pragma unroll
+      for (int u = 0; u < 3; u++) {
+        const int e = t + 256 * u;
+        v[u] = 0.0;
+        if (e < m * 16) {
+          const int r = c0 + 16 + (e >> 4), c = e & 15;
+          double s = 0.0;
+          for (int kk = 0; kk <= c; kk++) s = fma(a[r][c0 + kk], x[c0 + c][c0 + kk], s);
+          v[u] = s;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < 3; u++) {
+        const int e = t + 256 * u;
+        if (e < m * 16) a[c0 + 16 + (e >> 4)][c0 + (e & 15)] = v[u];
+      }
+    }
     __syncthreads();
-    {  // trailing triangle: row t / 4, columns j+1 + (t % 4) + 4i up to the diagonal
-      const int r = t >> 2, q = t & 3;
-      if (r > j) {
-        const double arj = a[r][j];
-        for (int c = j + 1 + q; c <= r; c += 4) a[r][c] = fma(-arj, a[c][j], a[r][c]);
+    for (int e = t; e < m * m; e += 256) {  // trailing triangle: A22 -= X X^T
+      const int r = c0 + 16 + e / m, s = c0 + 16 + e % m;
+      if (s > r) continue;
+      double acc = a[r][s];
+#pragma unroll
+      for (int kk = 0; kk < 16; kk++) acc -= a[r][c0 + kk] * a[s][c0 + kk];
+      a[r][s] = acc;
+    }
+    __syncthreads();
+  }
+  // off-diagonal blocks of inv(L): T = sum_k L_ik X_kj into block (i, j), then X_ij = -X_ii T
+  for (int d = 1; d < 4; d++) {
+    const int pairs = 4 - d;
+    double v[3];
+#pragma unroll
+    for (int u = 0; u < 3; u++) {
+      const int e = t + 256 * u;
+      v[u] = 0.0;
+      if (e < pairs * 256) {
+        const int jb = e >> 8, ib = jb + d, r = (e >> 4) & 15, c = e & 15;
+        double s = 0.0;
+        for (int kk = 16 * jb; kk < 16 * ib; kk++) s = fma(a[16 * ib + r][kk], x[kk][16 * jb + c], s);
+        v[u] = s;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 3; u++) {
+      const int e = t + 256 * u;
+      if (e < pairs * 256) {
+        const int jb = e >> 8, ib = jb + d, r = (e >> 4) & 15, c = e & 15;
+        x[16 * ib + r][16 * jb + c] = v[u];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 3; u++) {
+      const int e = t + 256 * u;
+      v[u] = 0.0;
+      if (e < pairs * 256) {
+        const int jb = e >> 8, ib = jb + d, r = (e >> 4) & 15, c = e & 15;
+        double s = 0.0;
+        for (int q = 0; q <= r; q++) s = fma(x[16 * ib + r][16 * ib + q], x[16 * ib + q][16 * jb + c], s);
+        v[u] = -s;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 3; u++) {
+      const int e = t + 256 * u;
+      if (e < pairs * 256) {
+        const int jb = e >> 8, ib = jb + d, r = (e >> 4) & 15, c = e & 15;
+        x[16 * ib + r][16 * jb + c] = v[u];
       }
     }
     __syncthreads();
   }
-  if (t < NB) a[t][t] = piv[t];
-  __syncthreads();
-  // in-place inverse of the lower-triangular block, columns right to left (LAPACK dtrti2)
-  const int g = t >> 2, q = t & 3;  // row group g (0..63), lane q within it
-  for (int j = NB - 1; j >= 0; j--) {
-    const double inv_jj = 1.0 / a[j][j];
-    const int i = g;
-    double acc = 0.0;
-    if (i > j)
-      for (int kk = j + 1 + q; kk <= i; kk += 4) acc = fma(a[i][kk], a[kk][j], acc);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    __syncthreads();
-    if (q == 0) {
-      if (i > j) a[i][j] = -inv_jj * acc;
-      else if (i == j) a[i][j] = inv_jj;
-    }
-    __syncthreads();
-  }
-  for (int i = t; i < NB * NB; i += 256) {
-    const int r = i / NB, c = i % NB;
-    A[(size_t)(k + r) * n + k + c] = (c <= r) ? a[r][c] : 0.0;
+  for (int i = t; i < 64 * 64; i += 256) {
+    const int r = i >> 6, c = i & 63;
+    A[(size_t)(k + r) * n + k + c] = (c <= r) ? x[r][c] : 0.0;
   }
 }
 
@@ -361,6 +468,17 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   const int n = fb.n, cnt = fb.count;
   if (cnt <= 0) return 0;
   if (n <= 0 || n % NB) return 2;
+  {  // the diagonal-block kernel's shared memory is above the 48 KB default (per device)
+    static unsigned long long opted = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+    if (!(opted & (1ULL << dev))) {
+      if (cudaFuncSetAttribute(potrf_inv_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kPotrfSmemBytes) != cudaSuccess)
+        return 1;
+      opted |= 1ULL << dev;
+    }
+  }
   for (int b = 0; b < cnt; b++) cudaMemsetAsync(fb.status[b], 0, sizeof(int), stream);
   {
     dim3 g((unsigned)((n + 255) / 256), (unsigned)n, (unsigned)cnt);
@@ -368,7 +486,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     note_launch();
   }
   for (int j = 0; j < n; j += NB) {
-    const int S = j > 0 ? ksplit(j) : 1;
+    const int S = j > 0 ? ksplit_batch(j, (n - j) / 64, cnt) : 1;
     if (j > 0) {
       chol_update_kernel<<<dim3((unsigned)((n - j) / 64), (unsigned)S, (unsigned)cnt), kFT, 0, stream>>>(fb, j, S);
       note_launch();
@@ -377,7 +495,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
         note_launch();
       }
     }
-    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, 0, stream>>>(fb, j);
+    potrf_inv_diag_kernel<<<(unsigned)cnt, 256, kPotrfSmemBytes, stream>>>(fb, j);
     note_launch();
     if (n - j - NB > 0) {
       trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), kFT, 0, stream>>>(fb, j);
@@ -388,7 +506,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   // blocks were inverted by the factorisation
   for (int j = n - 2 * NB; j >= 0; j -= NB) {
     const unsigned tiles = (unsigned)((n - j - NB + 63) / 64);
-    const int S = ksplit(n - j - NB);
+    const int S = ksplit_batch(n - j - NB, (int)tiles, cnt);
     trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), kFT, 0, stream>>>(fb, j, S);
     note_launch();
     if (S > 1) {

@@ -72,14 +72,15 @@ class Encoder:
         self._fstreams = None
 
     # ---------------------------------------------------------------- factorisation
-    def factor(self, hessians, diags=None, _max_tries=6, check=True, ready_events=None):
+    def factor(self, hessians, diags=None, _max_tries=6, check=True, ready_events=None, start_event=None):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
         Returns {key: Factor}.  All first attempts go out as one batched call (same-size
         Hessians advance through each factorisation step in a single launch); the status
         words are read with one synchronisation and only a non-positive pivot triggers the
         reference's damp escalation for that Hessian.  ready_events: {n: CUDA event} after
         which the Hessians of size n are on the device (each size's chain waits for its own
-        event instead of for everything queued on this stream)."""
+        event instead of for everything queued on this stream).  start_event: the point of
+        this stream the other chains wait for (default: everything queued so far)."""
         torch = self.torch
         L = nat.lib()
         keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
@@ -99,8 +100,11 @@ class Encoder:
         main = self.stream if self.stream is not None else torch.cuda.current_stream()
         status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
         slot = {k: i for i, k in enumerate(keys)}
-        ready = torch.cuda.Event()
-        ready.record(main)
+        if start_event is not None:
+            ready = start_event
+        else:
+            ready = torch.cuda.Event()
+            ready.record(main)
         out = {}
         self._factor_done = {}
         # Each size group is one chain of batched steps on its own stream; the largest (the
@@ -170,10 +174,21 @@ class Encoder:
         event after which the weights are ready (e.g. copies on another stream); the
         factorisations, which need only the Hessians, do not wait for it.  ready_events: as
         in factor()."""
-        factors = self.factor(hessians, diags, check=False, ready_events=ready_events)
+        main = self.stream if self.stream is not None else self.torch.cuda.current_stream()
+        start = self.torch.cuda.Event()
+        start.record(main)   # the Hessians are ready at this point of the stream
         if inputs_event is not None:
-            (self.stream if self.stream is not None else self.torch.cuda.current_stream()).wait_event(inputs_event)
-        raws, st = self.encode(jobs, factors, stats=stats, outputs=outputs, factor_event=self._factor_done)
+            main.wait_event(inputs_event)
+        made = {}
+
+        def launch_factor():
+            made["f"] = self.factor(hessians, diags, check=False, ready_events=ready_events, start_event=start)
+            return made["f"], self._factor_done
+
+        # the fits go out first, then the host launches the factor chains (side streams,
+        # higher priority) while the GPU already works on the fits
+        raws, st = self.encode(jobs, None, stats=stats, outputs=outputs, factor_fn=launch_factor)
+        factors = made["f"] if "f" in made else launch_factor()[0]
         redone = set(self.escalate(factors))
         if redone:
             again = [j for j in jobs if j.mode == "EF" and j.hkey in redone]
@@ -241,9 +256,10 @@ class Encoder:
         self._arena_key, self._arena_views = key, views
         return views
 
-    def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None):
+    def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None, factor_fn=None):
         """Encode every job with grouped launches; returns ({name: raw uint8 on device},
-        {name: stats dict})."""
+        {name: stats dict}).  factor_fn: called (instead of passing factors) once the first
+        round's fits and grids are queued; returns (factors, factor_event)."""
         torch = self.torch
         L = nat.lib()
         s = nat.stream_ptr(torch, self.stream)
@@ -327,6 +343,8 @@ class Encoder:
                                          nat.addr(views[i]["dl"]), nat.addr(views[i]["ml"]) if hm else None, None,
                                          int(j.x.shape[0]), int(j.x.shape[1]), pitch.get(i, 0)))
             block_call(L.cp_grid_params_batch, grid, "grid_params_batch")
+            if it == 0 and factor_fn is not None:
+                factors, factor_event = factor_fn()
             # The first round's sweeps go out per Hessian size as soon as that size's factors
             # (side streams, factor_event {n: event}) are done, smallest first, so they overlap
             # the larger factorisations; later rounds sweep everything in one launch.
