@@ -459,47 +459,103 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
                            dtype=torch.uint8).pin_memory()
     h2d = host_w.numel() * 2 + sum(v.numel() * 2 for v in host_h16.values()) + host_d32.numel() * 4
     d2h = sum(all_sizes) if rank == 0 else 0
-    copy_stream = torch.cuda.Stream()
-    hcopy_stream = torch.cuda.Stream(priority=-1)   # its decodes must not queue behind the fits
+    # every host-to-device copy goes out in order on one stream, so the link never waits for
+    # a kernel; the Hessian decodes and the weight conversions run on high-priority streams
+    # (they must not queue behind the fits and the factor chains) that wait for their copy
+    xfer = torch.cuda.Stream()
+    hcopy_stream = torch.cuda.Stream(priority=-1)
+    conv_stream = torch.cuda.Stream(priority=-1)
     hs_ = nat.stream_ptr(torch, hcopy_stream)
     # the stored diagonal is exact float32 and the decoded H carries it unchanged, so the
     # host copy gives act order and damping without reading H back
     hd = host_d32.numpy().astype(np.float64)
     host_diag = {k: hd[d_off[k]:d_off[k] + int(wl.hess[k].shape[0])] for k in keys}
+    # the weights travel in about twelve chunks cut at tensor boundaries; each chunk's round-1
+    # fits start once that chunk is on the device and converted.  Chunks holding a tensor
+    # without EF (token_embd: two fits, the largest fit work per byte) go first, so that the
+    # chunk arriving last leaves little fit work behind it.
+    names = [wl.uid(u) for u in wl.units]
+    counts = [(u.r1 - u.r0) * wl.spec_by_name[u.name].n for u in wl.units]
+    plain = {wl.uid(u) for u in wl.units if wl.spec_by_name[u.name].mode != "EF"}
+    chunks, cur, acc, off = [], [], 0, 0
+    target = max(1, sum(counts) // 12)
+    for nm, c in zip(names, counts):
+        if cur and (nm in plain) != any(x in plain for x in cur):
+            chunks.append((off, off + acc, cur))
+            off, cur, acc = off + acc, [], 0
+        cur.append(nm)
+        acc += c
+        if acc >= target:
+            chunks.append((off, off + acc, cur))
+            off, cur, acc = off + acc, [], 0
+    if cur:
+        chunks.append((off, off + acc, cur))
+    chunks.sort(key=lambda ch: (not any(x in plain for x in ch[2]), -(ch[1] - ch[0])))
+    d2h_stream = torch.cuda.Stream()
 
     def step():
-        # PCIe order: all diagonals (the fits' imatrix), the Hessians largest size first
-        # (each size's factor chain starts as soon as its Hessians are decoded), then the
-        # weights, which only the fits wait for.
+        # PCIe order: all diagonals (the fits' imatrix), the largest Hessians (the longest
+        # factor chain starts as soon as they are decoded), the first weight chunk, then the
+        # other Hessian sizes and the remaining weight chunks; every chunk's fits wait only
+        # for that chunk.
         sizes = sorted(by_size, reverse=True)
         ready = {}
 
-        def hessians(ns):
-            with torch.cuda.stream(hcopy_stream):
-                for n in ns:
-                    dev_h16[n].copy_(host_h16[n], non_blocking=True)
-                    for k in by_size[n]:
-                        nat.check(nat.lib().cp_hessian_decode(
-                            dev_h16[n].data_ptr() + 2 * h_off[k], dev_d32.data_ptr() + 4 * d_off[k],
-                            float(hscale[k]), n, nat.ptr(dev_H[k]), hs_), "hessian_decode")
-                    ready[n] = torch.cuda.Event()
-                    ready[n].record(hcopy_stream)
+        def arrived():
+            e = torch.cuda.Event()
+            e.record(xfer)
+            return e
 
-        hcopy_stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(hcopy_stream):
+        def hessians(ns):
+            for n in ns:
+                with torch.cuda.stream(xfer):
+                    dev_h16[n].copy_(host_h16[n], non_blocking=True)
+                hcopy_stream.wait_event(arrived())
+                for k in by_size[n]:
+                    nat.check(nat.lib().cp_hessian_decode(
+                        dev_h16[n].data_ptr() + 2 * h_off[k], dev_d32.data_ptr() + 4 * d_off[k],
+                        float(hscale[k]), n, nat.ptr(dev_H[k]), hs_), "hessian_decode")
+                ready[n] = torch.cuda.Event()
+                ready[n].record(hcopy_stream)
+
+        staged = []
+
+        def weights(part):
+            for a, b, nms in part:
+                with torch.cuda.stream(xfer):
+                    dev_w16[a:b].copy_(host_w[a:b], non_blocking=True)
+                conv_stream.wait_event(arrived())
+                with torch.cuda.stream(conv_stream):
+                    wl.x_flat[a:b].copy_(dev_w16[a:b])
+                ev = torch.cuda.Event()
+                ev.record(conv_stream)
+                staged.append((ev, nms))
+
+        cur_s = torch.cuda.current_stream()
+        for st_ in (xfer, hcopy_stream, conv_stream):
+            st_.wait_stream(cur_s)
+        with torch.cuda.stream(xfer):
             dev_d32.copy_(host_d32, non_blocking=True)
+        hcopy_stream.wait_event(arrived())
+        with torch.cuda.stream(hcopy_stream):
             for k in wl.qw:
                 wl.qw[k].copy_(dev_d32[d_off[k]:d_off[k] + wl.qw[k].numel()])
-        hessians(sizes)
-        copy_stream.wait_stream(hcopy_stream)
-        with torch.cuda.stream(copy_stream):
-            dev_w16.copy_(host_w, non_blocking=True)
-            wl.x_flat.copy_(dev_w16)
-            weights_ready = torch.cuda.Event()
-            weights_ready.record(copy_stream)
+        qw_ready = torch.cuda.Event()   # the fits read these imatrix means
+        qw_ready.record(hcopy_stream)
+        cur_s.wait_event(qw_ready)
+        hessians(sizes[:1])
+        weights(chunks[:1])
+        hessians(sizes[1:])
+        weights(chunks[1:])
         hs = {k: dev_H[k] for k in wl.ef_keys}
+
+        def copy_out(ev, _names):   # one GPU: the bytes leave while the statistics run
+            d2h_stream.wait_event(ev)
+            with torch.cuda.stream(d2h_stream):
+                host_out[:my_bytes].copy_(flat[:my_bytes], non_blocking=True)
+
         enc.run(jobs, hs, {k: host_diag[k] for k in wl.ef_keys}, stats=True, outputs=outputs,
-                inputs_event=weights_ready, ready_events=ready)
+                inputs_event=staged, ready_events=ready, after_pack=copy_out if world == 1 else None)
         if world > 1:
             bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
             if rank == 0:
@@ -507,8 +563,6 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
                 for b in bufs:
                     host_out[off:off + b.numel()].copy_(b[:b.numel()], non_blocking=True)
                     off += b.numel()
-        else:
-            host_out[:my_bytes].copy_(flat[:my_bytes], non_blocking=True)
         torch.cuda.synchronize()
 
     for _ in range(max(1, min(args.warmup, 2))):

@@ -204,6 +204,13 @@ typedef struct {
   int32_t elem_bytes;
 } cp_transpose_job;
 int cp_transpose_batch(const cp_transpose_job* jobs, int count, void* stream);
+
+/* Copy `bytes` from pinned host memory (cudaHostAlloc / page-locked, hence mapped) to device
+ * memory with a kernel that reads the host buffer over the bus.  Stream-ordered like
+ * cudaMemcpyAsync, but it does not wait behind copy-engine transfers queued earlier on other
+ * streams (the factorisation's act orders use it so that they are not held up by a bulk
+ * weight upload).  CP_ERR_ARG if src_host is not pinned. */
+int cp_fetch_host(void* dst, const void* src_host, int64_t bytes, void* stream);
 int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream);
 
 typedef struct {

@@ -112,6 +112,7 @@ def lib():
         "cp_ef_sweep_noalloc": ([I, P, I64, I64, P, P, P, P, P, P, P], I),
         "cp_ef_sweep_rows": ([I64], I64),
         "cp_transpose_batch": ([P, I, P], I),
+        "cp_fetch_host": ([P, P, I64, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

@@ -481,6 +481,19 @@ int cp_transpose_batch(const cp_transpose_job* jobs, int count, void* stream) {
   return CP_OK;
 }
 
+int cp_fetch_host(void* dst, const void* src_host, int64_t bytes, void* stream) {
+  if (bytes < 0) return set_err(CP_ERR_SHAPE, "cp_fetch_host: negative size");
+  if (bytes == 0) return CP_OK;
+  if (!dst || !src_host) return set_err(CP_ERR_ARG, "null pointer");
+  void* mapped = nullptr;
+  if (cudaHostGetDevicePointer(&mapped, const_cast<void*>(src_host), 0) != cudaSuccess || !mapped) {
+    cudaGetLastError();
+    return set_err(CP_ERR_ARG, "cp_fetch_host: the source is not pinned (mapped) host memory");
+  }
+  ProfScope ps(kProfOther, (cudaStream_t)stream);
+  return check_rc(cpk::launch_fetch_host(dst, mapped, bytes, (cudaStream_t)stream), "cp_fetch_host");
+}
+
 int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream) {
   if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
   cudaStream_t s = (cudaStream_t)stream;

@@ -89,6 +89,37 @@ __global__ void __launch_bounds__(256) transpose_u8_kernel(const __grid_constant
   }
 }
 
+// Copy from pinned host memory read directly by the kernel over the bus (mapped memory):
+// unlike a copy-engine transfer, it does not queue behind large transfers issued earlier on
+// other streams.  16-byte words when both ends are aligned, bytes otherwise.
+__global__ void __launch_bounds__(256) fetch_host_kernel(void* __restrict__ dst, const void* __restrict__ src,
+                                                         int64_t bytes) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = bytes >> 4;
+    const uint4* s4 = static_cast<const uint4*>(src);
+    uint4* d4 = static_cast<uint4*>(dst);
+    for (int64_t i = t0; i < n16; i += stride) d4[i] = s4[i];
+    done = n16 << 4;
+  }
+  const uint8_t* s1 = static_cast<const uint8_t*>(src);
+  uint8_t* d1 = static_cast<uint8_t*>(dst);
+  for (int64_t i = done + t0; i < bytes; i += stride) d1[i] = s1[i];
+}
+
+int launch_fetch_host(void* dst, const void* src_mapped, int64_t bytes, cudaStream_t stream) {
+  if (bytes <= 0) return 0;
+  int64_t blocks = ((bytes >> 4) + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 1184) blocks = 1184;
+  fetch_host_kernel<<<(unsigned)blocks, 256, 0, stream>>>(dst, src_mapped, bytes);
+  note_launch();
+  return 0;
+}
+
 int transpose_tile_dim(int elem_bytes) { return elem_bytes == 1 ? 128 : 64; }
 
 int64_t transpose_tiles(int64_t rows, int64_t cols, int elem_bytes) {

@@ -20,4 +20,6 @@ struct TrBatch {
 int transpose_tile_dim(int elem_bytes);
 int64_t transpose_tiles(int64_t rows, int64_t cols, int elem_bytes);
 int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles, cudaStream_t stream);
+// bytes from mapped (pinned) host memory to device memory, read by a kernel
+int launch_fetch_host(void* dst, const void* src_mapped, int64_t bytes, cudaStream_t stream);
 }  // namespace cpk

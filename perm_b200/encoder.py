@@ -125,9 +125,12 @@ class Encoder:
                 mean_diag = float(np.mean(np.asarray(diag, np.float64)[order]))
                 shifts.append(float(self.damp * (mean_diag if mean_diag > 0.0 else 1.0) + 1e-8))
             with torch.cuda.stream(st):
-                od = oh.to("cuda", non_blocking=True)
+                od = torch.empty((len(grp), n), dtype=torch.int32, device="cuda")
                 Ug = torch.empty((len(grp), n, n), dtype=torch.float32, device="cuda")
                 ut2g = torch.empty((len(grp), L.cp_ef_u_bytes(n) // 4), dtype=torch.float32, device="cuda")
+            # the act orders leave the pinned staging row through a kernel read, not a copy
+            # engine, so they never wait behind bulk uploads queued on other streams
+            nat.check(L.cp_fetch_host(nat.ptr(od), oh.data_ptr(), od.numel() * 4, sp), "fetch_host")
             for t_ in (od, Ug, ut2g):   # also read on the main stream (sweeps)
                 t_.record_stream(main)
             jobs = []
@@ -166,18 +169,26 @@ class Encoder:
             redone.append(k)
         return redone
 
-    def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None, ready_events=None):
+    def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None, ready_events=None,
+            after_pack=None):
         """factor() + encode() with the factorisations overlapped with the round-1 fits: the
         factor chains start on side streams, the fits (which need no U) go first on this
         stream, and the status words are read once at the end; tensors whose Hessian needed
         damp escalation are encoded again with the escalated factor.  inputs_event: a CUDA
-        event after which the weights are ready (e.g. copies on another stream); the
-        factorisations, which need only the Hessians, do not wait for it.  ready_events: as
-        in factor()."""
+        event after which the weights are ready (e.g. copies on another stream), or a list of
+        (event, job names) in arrival order, each group's first fits waiting only for its own
+        event; the factorisations, which need only the Hessians, wait for neither.
+        ready_events: as in factor().  after_pack(event, names): called as soon as the packed
+        bytes of the named jobs are queued (event: recorded after them on this stream),
+        before the statistics and the status read, so a caller can start copying them out;
+        called again for the jobs re-encoded after a damp escalation."""
         main = self.stream if self.stream is not None else self.torch.cuda.current_stream()
         start = self.torch.cuda.Event()
         start.record(main)   # the Hessians are ready at this point of the stream
-        if inputs_event is not None:
+        staged = None
+        if isinstance(inputs_event, (list, tuple)):
+            staged = inputs_event
+        elif inputs_event is not None:
             main.wait_event(inputs_event)
         made = {}
 
@@ -187,12 +198,14 @@ class Encoder:
 
         # the fits go out first, then the host launches the factor chains (side streams,
         # higher priority) while the GPU already works on the fits
-        raws, st = self.encode(jobs, None, stats=stats, outputs=outputs, factor_fn=launch_factor)
+        raws, st = self.encode(jobs, None, stats=stats, outputs=outputs, factor_fn=launch_factor,
+                               staged_inputs=staged, after_pack=after_pack)
         factors = made["f"] if "f" in made else launch_factor()[0]
         redone = set(self.escalate(factors))
         if redone:
             again = [j for j in jobs if j.mode == "EF" and j.hkey in redone]
-            r2, s2 = self.encode(again, factors, stats=stats, outputs={j.name: raws[j.name] for j in again})
+            r2, s2 = self.encode(again, factors, stats=stats, outputs={j.name: raws[j.name] for j in again},
+                                 after_pack=after_pack)
             st.update(s2)
         return raws, st
 
@@ -256,10 +269,13 @@ class Encoder:
         self._arena_key, self._arena_views = key, views
         return views
 
-    def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None, factor_fn=None):
+    def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None, factor_fn=None,
+               staged_inputs=None, after_pack=None):
         """Encode every job with grouped launches; returns ({name: raw uint8 on device},
         {name: stats dict}).  factor_fn: called (instead of passing factors) once the first
-        round's fits and grids are queued; returns (factors, factor_event)."""
+        round's fits and grids are queued; returns (factors, factor_event).  staged_inputs:
+        [(event, job names)], the weights of each group ready after its event.  after_pack:
+        as in run()."""
         torch = self.torch
         L = nat.lib()
         s = nat.stream_ptr(torch, self.stream)
@@ -308,25 +324,39 @@ class Encoder:
             return out
 
         # round 1 fits (EF from x) together with the weighted-RTN fits
-        items = []
-        for i, j in enumerate(jobs):
-            if j.mode == "EF":
-                items.append((j.ttype, j.x, j.qw, raws[i]))
-            elif j.mode == "wRTN(attn0-diag)":
-                items.append((j.ttype, j.x, j.fit_w, raws[i]))
-                if stats:
-                    items.append((j.ttype, j.x, j.qw, views[i]["base"].view(raws[i].shape)))
-            elif j.mode == "wRTN":
-                items.append((j.ttype, j.x, j.qw, raws[i]))
-            else:
-                raise ValueError(f"unknown mode {j.mode}")
-        fit_batch(items)
+        def round1_items(idx):
+            items = []
+            for i in idx:
+                j = jobs[i]
+                if j.mode == "EF":
+                    items.append((j.ttype, j.x, j.qw, raws[i]))
+                elif j.mode == "wRTN(attn0-diag)":
+                    items.append((j.ttype, j.x, j.fit_w, raws[i]))
+                    if stats:
+                        items.append((j.ttype, j.x, j.qw, views[i]["base"].view(raws[i].shape)))
+                elif j.mode == "wRTN":
+                    items.append((j.ttype, j.x, j.qw, raws[i]))
+                else:
+                    raise ValueError(f"unknown mode {j.mode}")
+            return items
+
+        main = self.stream if self.stream is not None else torch.cuda.current_stream()
+        if staged_inputs:
+            slot = {j.name: i for i, j in enumerate(jobs)}
+            left = set(range(len(jobs)))
+            for ev, names in staged_inputs:
+                idx = [slot[nm] for nm in names if nm in slot and slot[nm] in left]
+                main.wait_event(ev)
+                fit_batch(round1_items(idx))
+                left.difference_update(idx)
+            fit_batch(round1_items(sorted(left)))
+        else:
+            fit_batch(round1_items(range(len(jobs))))
         if stats:  # stock baseline = round-1 committed bytes (EF) or the separate qw fit (attn0)
             block_call(L.cp_weighted_err_batch, werr_items(ef_idx, 1), "weighted_err_batch")
             block_call(L.cp_weighted_err_batch,
                        werr_items([i for i, j in enumerate(jobs) if j.mode == "wRTN(attn0-diag)"], 1, True),
                        "weighted_err_batch")
-        main = self.stream if self.stream is not None else torch.cuda.current_stream()
         if cm:  # the sweep's weights column-major, once for every round
             transpose([(nat.addr(jobs[i].x), nat.addr(views[i]["xt"]), int(jobs[i].x.shape[0]),
                         int(jobs[i].x.shape[1]), int(jobs[i].x.shape[1]), pitch[i], 4) for i in ef_idx],
@@ -396,6 +426,10 @@ class Encoder:
                 rp.append(nat.BlockJob(TYPE_ID[j.ttype], None, nat.addr(raws[i]), nat.addr(views[i]["codes"]),
                                        None, None, None, None, None, int(j.x.shape[0]), int(j.x.shape[1])))
             block_call(L.cp_kquant_repack_batch, rp, "repack_batch")
+        if after_pack is not None:
+            packed = torch.cuda.Event()
+            packed.record(main)
+            after_pack(packed, [j.name for j in jobs])
         st = {}
         if stats:
             block_call(L.cp_weighted_err_batch, werr_items(range(len(jobs)), 0), "weighted_err_batch")

@@ -95,3 +95,52 @@ def test_run_escalates_damp_for_an_indefinite_hessian(orc):
         got = raws[name].cpu().numpy()
         frac = float(np.mean(orc.codes(tt, got, *W.shape) == orc.codes(tt, want, *W.shape)))
         assert frac >= 0.999, f"{name}: codes identical {frac:.4%}"
+
+
+def test_run_with_staged_weights_matches_resident():
+    """Encoder.run with the weights arriving in groups on another stream (a list of (event,
+    job names), each group's first fits waiting only for its own event) gives the same bytes
+    as a run whose weights were on the device from the start."""
+    import torch
+    from perm_b200.encoder import Encoder, Job
+    rng = np.random.default_rng(21)
+    hess = {"a": _hessian(rng, 256), "b": _hessian(rng, 512)}
+    hd = {k: torch.from_numpy(H).cuda() for k, H in hess.items()}
+    diags = {k: np.diag(H) for k, H in hess.items()}
+    specs = []
+    for i in range(6):
+        hk = "a" if i % 2 == 0 else "b"
+        W = (rng.standard_normal((96 + 32 * i, hess[hk].shape[0])) * 0.02).astype(np.float32)
+        specs.append((f"t{i}", ["Q2_K", "Q3_K", "Q6_K"][i % 3], W, np.diag(hess[hk]).astype(np.float32), hk))
+    Wemb = (rng.standard_normal((77, 256)) * 0.02).astype(np.float32)
+    fw = torch.from_numpy(np.diag(hess["a"]).astype(np.float32)).cuda()
+
+    def jobs_for(dev_w):
+        js = [Job(nm, tt, "EF", dev_w[nm], torch.from_numpy(qw).cuda(), hk) for nm, tt, _, qw, hk in specs]
+        js.append(Job("embd", "Q2_K", "wRTN(attn0-diag)", dev_w["embd"], None, None, fit_w=fw))
+        return js
+
+    host = {nm: torch.from_numpy(W).pin_memory() for nm, _, W, _, _ in specs}
+    host["embd"] = torch.from_numpy(Wemb).pin_memory()
+    resident = {nm: h.cuda() for nm, h in host.items()}
+    want, st_want = Encoder().run(jobs_for(resident), hd, diags)
+    want = {k: v.cpu().numpy() for k, v in want.items()}
+
+    staged_w = {nm: torch.empty_like(resident[nm]) for nm in host}
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    groups = [["t3", "embd"], ["t0", "t1", "t2"], ["t4", "t5"]]
+    staged = []
+    with torch.cuda.stream(side):
+        for g in groups:
+            for nm in g:
+                staged_w[nm].copy_(host[nm], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            staged.append((ev, g))
+    got, st_got = Encoder().run(jobs_for(staged_w), hd, diags, inputs_event=staged)
+    for nm in want:
+        assert np.array_equal(got[nm].cpu().numpy(), want[nm]), nm
+    assert set(st_got) == set(st_want)
+    for k in st_want:   # float64 sums reduced on the device in no fixed order
+        assert st_got[k]["rel_err_vs_stock"] == pytest.approx(st_want[k]["rel_err_vs_stock"], rel=1e-9, abs=1e-12)
