@@ -134,18 +134,10 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     }
     __syncthreads();
 
-    // 1. the block's working values, w = x[row, order[j0 + c]], and the grid values of the
-    // panel's first 16 columns (they land while step 2 runs)
+    // 1. the block's working values, w = x[row, order[j0 + c]]
     float w[kSwB];
 #pragma unroll
     for (int c = 0; c < kSwB; c++) w[c] = rv ? __ldg(xr + sm.ord[c] * cs) : 0.0f;
-    float pd[16], pm[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const int sidx = sm.ord[i] / sbw;
-      pd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
-      pm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
-    }
 
     // 2. errors of every earlier column, ascending jj
     for (int s = 0; s < nst; s++) {
@@ -172,8 +164,10 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
     // updates of the later columns of the sub-panel; then the 16 errors update the block's
     // remaining 16-column groups (ascending jj, packed); then w shifts down by 16 registers so
     // the next sub-panel again finds its columns in w[0..15].  Register indices stay
-    // compile-time and no update is computed that the reference does not make.
-    // dl/ml of sub-panel p + 1 are fetched while sub-panel p runs
+    // compile-time and no update is computed that the reference does not make.  The grid
+    // values are loaded at the start of each sub-panel: keeping the next sub-panel's in
+    // registers costs the fourth resident CTA per SM, which hides more latency than the
+    // prefetch does.
 #pragma unroll 1
     for (int p = 0; p < kSwB / 16; p++) {
       const int a0 = 16 * p;
@@ -181,16 +175,9 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
       float cd[16], cm[16];
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        cd[i] = pd[i];
-        cm[i] = pm[i];
-      }
-      if (p + 1 < kSwB / 16) {
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int sidx = sm.ord[a0 + 16 + i] / sbw;
-          pd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
-          pm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
-        }
+        const int sidx = sm.ord[a0 + i] / sbw;
+        cd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
+        cm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
       }
 #pragma unroll
       for (int i = 0; i < 16; i++) {
@@ -233,7 +220,7 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
   }
 }
 
-__global__ void __launch_bounds__(kSwThreads, 3) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+__global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
   int lo = 0, hi = b.count - 1;
   const int cta = blockIdx.x;
   while (lo < hi) {
