@@ -197,28 +197,40 @@ __device__ __forceinline__ float select_idx(const float (&x)[N], int idx) {
 // candidates.  w holds the weights (the caller passes x*x when the reference uses qw=None).
 // Returns the scale; L receives the codes as floats offset by +nmax.
 template <int N>
-__device__ __forceinline__ float fit_qx(const float (&x)[N], const float (&w)[N], int nmax, float (&L)[N]) {
+// The per-candidate sums run on packed pairs (f32x2; nz = -0.0 from a kernel argument).
+__device__ __forceinline__ float fit_qx(const float (&x)[N], const float (&w)[N], int nmax, float (&L)[N],
+                                       float nz) {
+  static_assert(N % 16 == 0, "pairs fill the 8 accumulators");
+  constexpr int P = N / 2;
   const int idx = argmax_abs(x);
   const float xm = select_idx(x, idx);
   const float amax = fabsf(xm);
   const bool dead = amax < kGroupEps;
   const float mx = dead ? 1.0f : xm;
-  float wx[N];
+  const f32x2 nz2 = pk2(nz, nz), magic2 = pk2(kMagic, kMagic);
+  f32x2 xp[P], wp[P], wxp[P];
 #pragma unroll
-  for (int i = 0; i < N; i++) wx[i] = w[i] * x[i];
+  for (int k = 0; k < P; k++) {
+    xp[k] = pk2(x[2 * k], x[2 * k + 1]);
+    wp[k] = pk2(w[2 * k], w[2 * k + 1]);
+    wxp[k] = mul2(wp[k], xp[k], nz2);  // wx = w * x
+  }
+  // sum(wx * l) and sum(w * l * l) for the codes l = clip(nearest_int(isc * x), -nmax, nmax - 1)
+  auto sums = [&](float isc, float& slx, float& sl2) {
+    const f32x2 isc2 = pk2(isc, isc);
+    Pw8x2 a, b;
+#pragma unroll
+    for (int k = 0; k < P; k++) {
+      const f32x2 lf = nint_clip2(mul2(isc2, xp[k], nz2), -nmax, nmax - 1, magic2);
+      a.addk(k, mul2(wxp[k], lf, nz2));
+      b.addk(k, mul2(mul2(wp[k], lf, nz2), lf, nz2));
+    }
+    slx = a.total();
+    sl2 = b.total();
+  };
   const float iscale = -(float)nmax / mx;
   float sumlx, suml2;
-  {
-    Pw8 a, b;
-#pragma unroll
-    for (int i = 0; i < N; i++) {
-      const float lf = nint_clip_f(iscale * x[i], -nmax, nmax - 1);
-      a.addi(i, wx[i] * lf);
-      b.addi(i, w[i] * lf * lf);
-    }
-    sumlx = a.total();
-    suml2 = b.total();
-  }
+  sums(iscale, sumlx, suml2);
   float scale = (suml2 != 0.0f) ? sumlx / suml2 : 0.0f;
   float best = scale * sumlx;
   float b_isc = iscale;
@@ -226,14 +238,8 @@ __device__ __forceinline__ float fit_qx(const float (&x)[N], const float (&w)[N]
   for (int s = -9; s <= 9; s++) {
     if (s == 0) continue;
     const float isc = -((float)nmax + 0.1f * (float)s) / mx;
-    Pw8 a, b;
-#pragma unroll
-    for (int i = 0; i < N; i++) {
-      const float lf = nint_clip_f(isc * x[i], -nmax, nmax - 1);
-      a.addi(i, wx[i] * lf);
-      b.addi(i, w[i] * lf * lf);
-    }
-    const float slx = a.total(), sl2 = b.total();
+    float slx, sl2;
+    sums(isc, slx, sl2);
     if (sl2 > 0.0f && slx * slx > best * sl2 && !dead) {
       const float ns = slx / sl2;
       scale = ns;

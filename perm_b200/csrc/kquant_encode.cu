@@ -235,14 +235,14 @@ __device__ __forceinline__ void q3k_encode_body(const float* __restrict__ x, con
 #pragma unroll
     for (int i = 0; i < 16; i++) w[i] = q[i] * sqrtf(sigma2 + xv[i] * xv[i]);
     const float sw = np_sum(w);
-    const float scale = fit_qx<16>(xv, w, 4, Lf);
+    const float scale = fit_qx<16>(xv, w, 4, Lf, nz);
     float vs[16], vw[16], Ls[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) {
       vs[j] = __shfl_sync(0xffffffffu, scale, j, 16);
       vw[j] = __shfl_sync(0xffffffffu, sw, j, 16);
     }
-    d = fit_qx<16>(vs, vw, 32, Ls);
+    d = fit_qx<16>(vs, vw, 32, Ls, nz);
     my_Ls = (int)select_idx(Ls, sub);
   } else {
     const float scale = fit_q3<16>(xv, 4, Lf);
@@ -330,7 +330,7 @@ __device__ __forceinline__ void q6k_encode_body(const float* __restrict__ x, con
 #pragma unroll
     for (int i = 0; i < 16; i++) w[i] = xv[i] * xv[i];
   }
-  const float scale = fit_qx<16>(xv, w, 32, Lf);
+  const float scale = fit_qx<16>(xv, w, 32, Lf, nz);
   float vs[16];
 #pragma unroll
   for (int j = 0; j < 16; j++) vs[j] = __shfl_sync(0xffffffffu, scale, j, 16);
