@@ -103,7 +103,8 @@ int cp_factor_u_f64(const double* H, int64_t n, const int32_t* order, double dia
 
 /* Device layout of U for the sweep: U row-major float32 [n][n] followed by its diagonal,
  * cp_ef_u_bytes(n) bytes (U and u_prepared 16-byte aligned).  Built once per factor (q/k/v
- * and gate/up share theirs). */
+ * and gate/up share theirs).  u_prepared may equal U (the factor written straight into the
+ * start of a cp_ef_u_bytes(n) buffer): then only the diagonal is appended. */
 size_t cp_ef_u_bytes(int64_t n);
 int cp_ef_prepare_u(const float* U, int64_t n, float* u_prepared, void* stream);
 

@@ -238,8 +238,19 @@ size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
 
 size_t ef_u_prepared_bytes(int64_t n) { return (size_t)n * (size_t)n * sizeof(float) + (size_t)n * sizeof(float); }
 
+// The factor already sits at the start of the prepared buffer (U == out): append the diagonal.
+__global__ void prepare_u_diag_kernel(float* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[(size_t)n * n + i] = out[(size_t)i * n + i];
+}
+
 int launch_prepare_u(const float* U, int64_t n, float* out, cudaStream_t stream) {
   if (n % 32) return 2;
+  if (U == out) {
+    prepare_u_diag_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(out, (int)n);
+    note_launch();
+    return 0;
+  }
   const size_t n4 = (size_t)n * n / 4;
   const int grid = (int)std::min<size_t>((n4 + 255) / 256, (size_t)148 * 8);
   prepare_u_kernel<<<grid, 256, 0, stream>>>(U, (int)n, out);

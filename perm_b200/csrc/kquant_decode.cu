@@ -321,13 +321,19 @@ __device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t c) {
   constexpr int SW = (T == kQ4_K || T == kQ5_K) ? 32 : 16;
   constexpr int NS = 256 / SW;
   constexpr int BB = block_bytes(T);
-  __shared__ uint8_t sraw[kSbPerCta * 210];
+  __shared__ __align__(16) uint8_t sraw[kSbPerCta * 210];
   __shared__ float sdl[kSbPerCta][16], sml[kSbPerCta][16];
   const int i = threadIdx.x;
   const int64_t sb0 = c * kSbPerCta;
   const int nsb = (int)min((int64_t)kSbPerCta, t.nsb - sb0);
   const uint8_t* src = t.raw + sb0 * BB;
-  for (int k = i; k < nsb * BB; k += 256) sraw[k] = src[k];
+  const int nbytes = nsb * BB;
+  if (((reinterpret_cast<uintptr_t>(src) | (uintptr_t)nbytes) & 3) == 0) {  // 4-byte words
+    const uint32_t* s4 = reinterpret_cast<const uint32_t*>(src);
+    for (int k = i; k < nbytes / 4; k += 256) reinterpret_cast<uint32_t*>(sraw)[k] = s4[k];
+  } else {
+    for (int k = i; k < nbytes; k += 256) sraw[k] = src[k];
+  }
   __syncthreads();
   if (i < nsb * NS) {
     const int k = i / NS, j = i % NS;
@@ -338,13 +344,15 @@ __device__ __forceinline__ void werr_sb(const SbDesc& t, int64_t c) {
   }
   __syncthreads();
   double acc = 0.0;
+  int64_t wrow = sb0 % t.nsb_row;  // superblock column of the weight row, stepped with wrap
+  const float* __restrict__ xs = t.x + sb0 * 256 + i;
   for (int k = 0; k < nsb; k++) {
-    const int64_t sb = sb0 + k;
     float v = sdl[k][i / SW] * (float)code_of<T>(sraw + k * BB, i);
     if (!(T == kQ3_K || T == kQ6_K)) v = v - sml[k][i / SW];
-    const float d = v - t.x[sb * 256 + i];
-    const float wt = t.w ? t.w[(sb % t.nsb_row) * 256 + i] : 1.0f;
+    const float d = v - xs[k * 256];
+    const float wt = t.w ? t.w[wrow * 256 + i] : 1.0f;
     acc += (double)(d * d * wt);
+    wrow = (wrow + 1 == t.nsb_row) ? 0 : wrow + 1;
   }
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   __shared__ double red[8];

@@ -126,18 +126,19 @@ class Encoder:
                 shifts.append(float(self.damp * (mean_diag if mean_diag > 0.0 else 1.0) + 1e-8))
             with torch.cuda.stream(st):
                 od = torch.empty((len(grp), n), dtype=torch.int32, device="cuda")
-                Ug = torch.empty((len(grp), n, n), dtype=torch.float32, device="cuda")
+                # U is written straight into the start of the sweep's prepared layout
                 ut2g = torch.empty((len(grp), L.cp_ef_u_bytes(n) // 4), dtype=torch.float32, device="cuda")
             # the act orders leave the pinned staging row through a kernel read, not a copy
             # engine, so they never wait behind bulk uploads queued on other streams
             nat.check(L.cp_fetch_host(nat.ptr(od), oh.data_ptr(), od.numel() * 4, sp), "fetch_host")
-            for t_ in (od, Ug, ut2g):   # also read on the main stream (sweeps)
+            for t_ in (od, ut2g):   # also read on the main stream (sweeps)
                 t_.record_stream(main)
             jobs = []
             for r, k in enumerate(grp):
-                jobs.append(nat.FactorJob(hessians[k].data_ptr(), n, od[r].data_ptr(), shifts[r], Ug[r].data_ptr(),
+                U = ut2g[r, :n * n].view(n, n)
+                jobs.append(nat.FactorJob(hessians[k].data_ptr(), n, od[r].data_ptr(), shifts[r], U.data_ptr(),
                                           self._fws[k].data_ptr(), status[slot[k]:slot[k] + 1].data_ptr()))
-                out[k] = Factor(Ug[r], ohn[r].astype(np.int64), od[r], self.damp, ut2g[r])
+                out[k] = Factor(U, ohn[r].astype(np.int64), od[r], self.damp, ut2g[r])
             arr = nat.job_array(nat.FactorJob, jobs)
             nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
             for k in grp:
