@@ -494,10 +494,10 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
     d2h_stream = torch.cuda.Stream()
 
     def step():
-        # PCIe order: all diagonals (the fits' imatrix), the largest Hessians (the longest
-        # factor chain starts as soon as they are decoded), the first weight chunk, then the
-        # other Hessian sizes and the remaining weight chunks; every chunk's fits wait only
-        # for that chunk.
+        # PCIe order: all diagonals (the fits' imatrix), the first weight chunk (token_embd:
+        # its two fits keep the GPU busy from the first milliseconds), the Hessians largest
+        # size first (the longest factor chain starts as soon as they are decoded), then the
+        # remaining weight chunks; every chunk's fits wait only for that chunk.
         sizes = sorted(by_size, reverse=True)
         ready = {}
 
@@ -543,8 +543,8 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
         qw_ready = torch.cuda.Event()   # the fits read these imatrix means
         qw_ready.record(hcopy_stream)
         cur_s.wait_event(qw_ready)
-        hessians(sizes[:1])
         weights(chunks[:1])
+        hessians(sizes[:1])
         hessians(sizes[1:])
         weights(chunks[1:])
         hs = {k: dev_H[k] for k in wl.ef_keys}
