@@ -112,6 +112,9 @@ __device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b, f32x2 nz2) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(nz2));
   return r;
 }
+// |v| on both halves (the sign bits cleared, as fabsf does).
+__device__ __forceinline__ f32x2 abs2(f32x2 v) { return v & 0x7FFFFFFF7FFFFFFFull; }
+
 // nint_clip_f on both halves: the magic add and subtract as pair operations, the clamp on
 // the bit patterns of each half.
 __device__ __forceinline__ f32x2 nint_clip2(f32x2 v, int lo, int hi, f32x2 magic2) {

@@ -11,12 +11,12 @@ namespace cpk {
 // Instead of copying the candidate codes on acceptance, the (iscale, min) pair that produced
 // them is recorded and the codes are recomputed once at the end (same arithmetic).
 // Outputs: scale, -min and the codes as floats (0..nmax).
-// The squared-error variant (MAD false) runs its candidate loop on packed pairs (f32x2, with
-// nz = -0.0 from a kernel argument) and keeps x - min in registers between acceptances.
+// The candidate loop runs on packed pairs (f32x2, with nz = -0.0 from a kernel argument) and
+// keeps x - min in registers between acceptances; MAD takes |d| by clearing the sign bits.
 template <int N, bool MAD, bool QKX3>
 __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N], int nmax, float rmin,
                                         float rdelta, int nstep, float& o_scale, float& o_negmin,
-                                        float (&Lf)[N], float nz = 0.0f) {
+                                        float (&Lf)[N], float nz) {
   float mn = x[0], mx = x[0];
 #pragma unroll
   for (int i = 1; i < N; i++) {
@@ -53,7 +53,7 @@ __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N]
   }
   float b_isc = iscale, b_mn = mn;
   bool b_fin = fin0;
-  if constexpr (!MAD) {
+  {
     static_assert(N % 16 == 0, "pairs fill the 8 accumulators");
     constexpr int P = N / 2;
     const f32x2 nz2 = pk2(nz, nz), magic2 = pk2(kMagic, kMagic);
@@ -99,7 +99,7 @@ __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N]
 #pragma unroll
         for (int k = 0; k < P; k++) {
           const f32x2 d = sub2(add2(mul2(ts2, lf[k], nz2), tm2), xp[k]);
-          pc.addk(k, mul2(wp[k], mul2(d, d, nz2), nz2));
+          pc.addk(k, mul2(wp[k], MAD ? abs2(d) : mul2(d, d, nz2), nz2));
         }
         const float cur = pc.total();
         if (cur < best) {
@@ -115,51 +115,6 @@ __device__ __forceinline__ void fit_qkx(const float (&x)[N], const float (&w)[N]
         }
       }
     }
-  } else {
-  float lf[N];
-  for (int step = 0; step <= nstep; step++) {
-    float span_cur = mx - mn;
-    span_cur = span_cur > 0.0f ? span_cur : 1.0f;
-    const float isc = (rmin + rdelta * (float)step + (float)nmax) / span_cur;
-    Pw8 sl, sl2, sxl;
-#pragma unroll
-    for (int i = 0; i < N; i++) {
-      lf[i] = nint_clip_f(isc * (x[i] - mn), 0, nmax);
-      const float wl = w[i] * lf[i];
-      sl.addi(i, wl);
-      sl2.addi(i, wl * lf[i]);
-      sxl.addi(i, wl * x[i]);
-    }
-    const float sum_l = sl.total(), sum_l2 = sl2.total(), sum_xl = sxl.total();
-    const float D = sum_w * sum_l2 - sum_l * sum_l;
-    // numpy: an infinite candidate scale gives all-zero codes, hence D == 0: never accepted.
-    const bool ok = D > 0.0f && isc <= 3.4028234663852886e38f;
-    if (ok && !dead) {
-      float this_scale = (sum_w * sum_xl - sum_x * sum_l) / D;
-      float this_min = (sum_l2 * sum_x - sum_l * sum_xl) / D;
-      const float alt_scale = sum_xl / sum_l2;
-      if (this_min > 0.0f) {
-        this_min = 0.0f;
-        this_scale = alt_scale;
-      }
-      Pw8 pc;
-#pragma unroll
-      for (int i = 0; i < N; i++) {
-        float d = this_scale * lf[i] + this_min - x[i];
-        d = MAD ? fabsf(d) : d * d;
-        pc.addi(i, w[i] * d);
-      }
-      const float cur = pc.total();
-      if (cur < best) {
-        best = cur;
-        scale = this_scale;
-        b_isc = isc;
-        b_mn = mn;
-        b_fin = true;
-        mn = this_min;
-      }
-    }
-  }
   }
 #pragma unroll
   for (int i = 0; i < N; i++)

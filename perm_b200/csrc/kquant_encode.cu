@@ -156,7 +156,7 @@ __device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, con
   } else {
 #pragma unroll
     for (int i = 0; i < 16; i++) w[i] = fabsf(xv[i]);
-    fit_qkx<16, true, false>(xv, w, 3, -0.5f, 0.1f, 15, scale, negmin, Lf);
+    fit_qkx<16, true, false>(xv, w, 3, -0.5f, 0.1f, 15, scale, negmin, Lf, nz);
     float max_scale = __shfl_sync(0xffffffffu, scale, 0, 16);
     float max_min = __shfl_sync(0xffffffffu, negmin, 0, 16);
 #pragma unroll
