@@ -385,9 +385,9 @@ def gpu_arm(args, rank, world, local_rank):
     if dom == "sweep":
         # DRAM bytes of one sweep launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) of
         # the second step's first sweep launch of this default workload on one B200 measured
-        # 36.41 GB (30.49 read + 5.92 written) for 425.1 G ordered updates, 0.08564 bytes per
+        # 36.77 GB (31.37 read + 5.40 written) for 425.1 G ordered updates, 0.08649 bytes per
         # update; per launch of this rank = that rate x this rank's updates per round
-        traffic = 0.08564 * alg["sweep_updates"] / max(1.0, nl)
+        traffic = 0.08649 * alg["sweep_updates"] / max(1.0, nl)
     roofline = {"kernel": {"fit": "kquant fit+pack", "sweep": "ef_sweep", "factor": "fp64 factor"}[dom],
                 "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
                 "frac": (gbs / hbm) if gbs is not None else None, "traffic": traffic,
