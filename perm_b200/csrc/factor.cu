@@ -60,6 +60,30 @@ __global__ void permute_reverse_kernel(const __grid_constant__ FactorBatch fb) {
   fb.P[b][(size_t)i * n + j] = v;
 }
 
+// Row-staged form of permute_reverse_kernel: the CTA reads its source row of H once, with
+// coalesced loads, into shared memory and gathers the permuted columns from there (the direct
+// form's scattered 8-byte reads move four times the bytes through L2).  blockIdx.x: row i of
+// P, blockIdx.y: item.  Used while a row (n doubles) fits in shared memory.
+constexpr int kPermRowSmemMax = 227 * 1024;
+__global__ void __launch_bounds__(256) permute_reverse_rows_kernel(const __grid_constant__ FactorBatch fb) {
+  extern __shared__ double hrow[];
+  const int n = fb.n, i = blockIdx.x, b = blockIdx.y;
+  const int* __restrict__ order = fb.order[b];
+  const double* __restrict__ src = fb.H[b] + (size_t)order[n - 1 - i] * n;
+  for (int c = threadIdx.x; c < n; c += 256) hrow[c] = src[c];
+  __syncthreads();
+  double* __restrict__ dst = fb.P[b] + (size_t)i * n;
+  const double sh = fb.shift[b];
+  for (int j = threadIdx.x; j < n; j += 256) {
+    double v = 0.0;
+    if (j <= i) {
+      v = hrow[order[n - 1 - j]];
+      if (i == j) v += sh;
+    }
+    dst[j] = v;
+  }
+}
+
 // Diagonal block at (k, k): Cholesky factor L11 of the (already updated) 64 x 64 block, then
 // its inverse, written in place of the block.  Nothing after this step needs L11 itself: the
 // panel below is solved with inv(L11) and the diagonal blocks of L^-1 are exactly these
@@ -468,19 +492,24 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   const int n = fb.n, cnt = fb.count;
   if (cnt <= 0) return 0;
   if (n <= 0 || n % NB) return 2;
-  {  // the diagonal-block kernel's shared memory is above the 48 KB default (per device)
+  {  // the diagonal-block and row-staged permute kernels use more than the 48 KB default (per device)
     static unsigned long long opted = 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
     if (!(opted & (1ULL << dev))) {
       if (cudaFuncSetAttribute(potrf_inv_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kPotrfSmemBytes) != cudaSuccess)
+                               kPotrfSmemBytes) != cudaSuccess ||
+          cudaFuncSetAttribute(permute_reverse_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kPermRowSmemMax) != cudaSuccess)
         return 1;
       opted |= 1ULL << dev;
     }
   }
   for (int b = 0; b < cnt; b++) cudaMemsetAsync(fb.status[b], 0, sizeof(int), stream);
-  {
+  if ((size_t)n * sizeof(double) <= (size_t)kPermRowSmemMax) {
+    permute_reverse_rows_kernel<<<dim3((unsigned)n, (unsigned)cnt), 256, (size_t)n * sizeof(double), stream>>>(fb);
+    note_launch();
+  } else {
     dim3 g((unsigned)((n + 255) / 256), (unsigned)n, (unsigned)cnt);
     permute_reverse_kernel<<<g, 256, 0, stream>>>(fb);
     note_launch();
