@@ -408,13 +408,29 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
   cudaStream_t s = (cudaStream_t)stream;
   static thread_local cpk::SweepBatch b;
+  // A launch too small to keep the GPU busy (under two waves of four resident 128-row CTAs per
+  // SM) is bounded by its longest rows, whose columns one lane walks serially; such a launch
+  // runs the column-split form, two warps per 32 rows, each applying the errors to half of
+  // every block.
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess || sms <= 0)
+      sms = 148;
+  }
+  int64_t plain = 0;
+  for (int i = 0; i < count; i++)
+    if (jobs[i].nrow > 0) plain += cpk::sweep_ctas(jobs[i].nrow);
+  const bool small_launch = plain < 2LL * 4 * sms;
   b.count = 0;
   int tiles = 0;
   for (int i = 0; i <= count; i++) {
     const bool flush = (i == count) || b.count == cpk::kSweepBatchMax;
     if (flush && b.count) {
       ProfScope ps(kProfSweep, s);
-      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, s), "cp_ef_sweep_batch")) return rc;
+      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, small_launch, s), "cp_ef_sweep_batch"))
+        return rc;
       b.count = 0;
       tiles = 0;
     }
@@ -435,7 +451,7 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
     if (j.pitch > (int64_t)1 << 31) return set_err(CP_ERR_SHAPE, "cp_ef_sweep_batch: pitch too large");
     d.pitch = (int)j.pitch;
     d.tile0 = tiles;
-    tiles += cpk::sweep_ctas(j.nrow);
+    tiles += small_launch ? cpk::sweep_split_ctas(j.nrow) : cpk::sweep_ctas(j.nrow);
     b.count++;
   }
   return CP_OK;

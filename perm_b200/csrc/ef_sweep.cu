@@ -73,12 +73,17 @@ struct SweepSmem {
   float dg[kSwB];                                    // U[j0+a][j0+a]
   int ord[kSwB];                                     // order[j0+a]
   __align__(16) float ru[kSwST][kSwJS][kSwB];        // ring: U[jj][j0 .. j0+63]
-  __align__(16) float re[kSwST][kSweepWarps][kSwJS][32];  // ring: errors e_jj of each warp's rows
+  union __align__(16) {
+    float re[kSwST][kSweepWarps][kSwJS][32];         // ring: errors e_jj of each warp's rows
+    struct {                                         // column-split form (sweep_rows_split)
+      float re[kSwST][2][kSwJS][32];                 // ring: errors e_jj of the CTA's two row tiles
+      float xb[2][32][32];                           // errors of block columns 0..31, per row tile
+    } cs;
+  };
 };
 
 // One CTA = kSweepWarps x 32 rows of one tensor.
-__device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz) {
-  __shared__ SweepSmem sm;
+__device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz, SweepSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = t.n, nrow = t.nrow;
   const int tile32 = cta * kSweepWarps + warp;
@@ -220,15 +225,185 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
   }
 }
 
-__global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+// Column-split form, for long rows in launches too small to fill the GPU: a CTA of four warps
+// owns 64 rows; warps 2p and 2p + 1 share rows 32p .. 32p + 31 (lane = row) and split every
+// 64-column block, warp h keeping block columns 32h .. 32h + 31 in registers.  Each warp
+// applies the earlier columns' errors to its half only, which halves the serial work of a
+// row.  In the panel, warp 0 of the pair quantizes columns 0..31 and hands their errors to
+// warp 1 through shared memory; warp 1 applies them in ascending order and then quantizes
+// columns 32..63.  Every element still receives exactly the reference's updates in the
+// reference's order, each rounded as the reference rounds it.
+__device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, float nz, SweepSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int pair = warp >> 1, h = warp & 1, cb = 32 * h;
+  const int n = t.n, nrow = t.nrow;
+  const int tile32 = cta * 2 + pair;
+  const int row = tile32 * 32 + lane;
+  const bool rv = row < nrow;
+  const int sbw = t.sbw, lo = t.lo, hi = t.hi, nsub = n / sbw;
+  const float* __restrict__ U = t.u;
+  const float* __restrict__ diagU = t.u + (size_t)n * n;
+  float* __restrict__ E = t.work;                              // [tile32][n][32]
+  const float* __restrict__ Ecta = t.work + (size_t)cta * 2 * n * 32;
+  float* __restrict__ Erow = E + (size_t)tile32 * n * 32 + lane;
+  const int64_t cs = t.pitch ? t.pitch : 1, rs = t.pitch ? 1 : n, rsg = t.pitch ? 1 : nsub;
+  const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * rs;
+  const float* __restrict__ dlr = t.dl + (size_t)(rv ? row : 0) * rsg;
+  const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * rsg : nullptr;
+  int8_t* __restrict__ codes = t.codes + (size_t)row * rs;
+  float* __restrict__ wout = t.wout ? t.wout + (size_t)row * rs : nullptr;
+
+  for (int j0 = 0; j0 < n; j0 += kSwB) {
+    __syncthreads();  // the previous block's readers of the shared buffers are done
+    const int nst = j0 / kSwJS;
+    // stage s = U rows jj in [s*JS, s*JS + JS) of this block's columns + the errors of those
+    // jj for the CTA's two row tiles (16 + 2 * 8 = 32 chunks of 16 bytes per jj)
+    auto issue = [&](int s) {
+      if (s < nst) {
+        const int st = s % kSwST, jj0 = s * kSwJS;
+        for (int c = tid; c < kSwJS * (16 + 8 * 2); c += kSwThreads) {
+          if (c < kSwJS * 16) {
+            const int k = c >> 4, c4 = c & 15;
+            cp_async16(&sm.ru[st][k][4 * c4], U + (size_t)(jj0 + k) * n + j0 + 4 * c4);
+          } else {
+            const int c2 = c - kSwJS * 16, w = c2 / (kSwJS * 8), rem = c2 % (kSwJS * 8);
+            const int k = rem >> 3, l4 = rem & 7;
+            cp_async16(&sm.cs.re[st][w][k][4 * l4], Ecta + ((size_t)w * n + jj0 + k) * 32 + 4 * l4);
+          }
+        }
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < kSwST - 1; s++) issue(s);
+    for (int i = tid; i < kSwB * kSwB / 4; i += kSwThreads) {
+      const int a = i >> 4, c4 = i & 15;
+      reinterpret_cast<float4*>(sm.ud[a])[c4] =
+          __ldg(reinterpret_cast<const float4*>(U + (size_t)(j0 + a) * n + j0) + c4);
+    }
+    if (tid < kSwB) {
+      sm.ord[tid] = __ldg(t.order + j0 + tid);
+      sm.dg[tid] = __ldg(diagU + j0 + tid);
+    }
+    __syncthreads();
+
+    // 1. this warp's half of the block, w = x[row, order[j0 + cb + c]]
+    float w[32];
+#pragma unroll
+    for (int c = 0; c < 32; c++) w[c] = rv ? __ldg(xr + sm.ord[cb + c] * cs) : 0.0f;
+
+    // 2. errors of every earlier column, ascending jj, on this warp's 32 columns
+    for (int s = 0; s < nst; s++) {
+      cp_async_wait<kSwST - 2>();
+      __syncthreads();  // stage s landed for everyone; everyone is done with stage s - 1
+      issue(s + kSwST - 1);
+      const int st = s % kSwST;
+#pragma unroll
+      for (int k = 0; k < kSwJS; k++) {
+        const float e = sm.cs.re[st][pair][k][lane];
+        const float4* u4 = reinterpret_cast<const float4*>(&sm.ru[st][k][cb]);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; c4++) {
+          const float4 u = u4[c4];
+          upd2(w[4 * c4], w[4 * c4 + 1], e, e, u.x, u.y, nz);
+          upd2(w[4 * c4 + 2], w[4 * c4 + 3], e, e, u.z, u.w, nz);
+        }
+      }
+    }
+    cp_async_wait<0>();
+
+    // 3. panel of this warp's half: two sub-panels of 16 (as in sweep_rows, with the later
+    // group of the half updated after the first); warp 0 also leaves its errors in xb
+    auto panel = [&]() {
+#pragma unroll 1
+      for (int p = 0; p < 2; p++) {
+        const int a0 = cb + 16 * p;
+        float es[16];
+        float cd[16], cm[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int sidx = sm.ord[a0 + i] / sbw;
+          cd[i] = rv ? __ldg(dlr + sidx * cs) : 0.0f;
+          cm[i] = (rv && mlr) ? __ldg(mlr + sidx * cs) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int a = a0 + i, j = sm.ord[a];
+          const float dlv = cd[i], mlv = cm[i], wa = w[i];
+          int q = 0;
+          float e = 0.0f;
+          if (dlv != 0.0f) {
+            q = clampi(nint((wa + mlv) / dlv), lo, hi);
+            const float recon = dlv * (float)q - mlv;
+            e = (wa - recon) / sm.dg[a];
+          }
+          if (rv) {
+            codes[j * cs] = (int8_t)q;
+            if (wout) wout[j * cs] = wa;
+          }
+          Erow[(size_t)(j0 + a) * 32] = e;
+          if (h == 0) sm.cs.xb[pair][a][lane] = e;
+          es[i] = e;
+#pragma unroll
+          for (int b = i + 1; b < 16; b++) w[b] = w[b] - e * sm.ud[a][a0 + b];
+        }
+        if (p == 0) {  // the half's second 16 columns (w[16..31])
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[a0 + i][a0 + 16]);
+#pragma unroll
+            for (int c2 = 0; c2 < 8; c2++) {
+              const float2 u = u2[c2];
+              upd2(w[16 + 2 * c2], w[16 + 2 * c2 + 1], es[i], es[i], u.x, u.y, nz);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 16; c++) w[c] = w[c + 16];
+        }
+      }
+    };
+    if (h == 0) panel();
+    __syncthreads();  // warp 0's errors of columns 0..31 are in xb
+    if (h == 1) {
+      // the errors of block columns 0..31, ascending, on columns 32..63
+#pragma unroll 4
+      for (int i = 0; i < 32; i++) {
+        const float e = sm.cs.xb[pair][i][lane];
+        const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[i][32]);
+#pragma unroll
+        for (int c2 = 0; c2 < 16; c2++) {
+          const float2 u = u2[c2];
+          upd2(w[2 * c2], w[2 * c2 + 1], e, e, u.x, u.y, nz);
+        }
+      }
+      panel();
+    }
+  }
+}
+
+__device__ __forceinline__ int sweep_desc_of(const SweepBatch& b, int cta) {
   int lo = 0, hi = b.count - 1;
-  const int cta = blockIdx.x;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (b.d[mid].tile0 <= cta) lo = mid;
     else hi = mid - 1;
   }
-  sweep_rows(b.d[lo], cta - b.d[lo].tile0, nz);
+  return lo;
+}
+
+__global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_batch_kernel(const __grid_constant__ SweepBatch b, float nz) {
+  __shared__ SweepSmem sm;
+  const int k = sweep_desc_of(b, blockIdx.x);
+  sweep_rows(b.d[k], blockIdx.x - b.d[k].tile0, nz, sm);
+}
+
+// The column-split form as its own kernel, so that neither form's register allocation
+// constrains the other.
+__global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_split_batch_kernel(const __grid_constant__ SweepBatch b,
+                                                                             float nz) {
+  __shared__ SweepSmem sm;
+  const int k = sweep_desc_of(b, blockIdx.x);
+  sweep_rows_split(b.d[k], blockIdx.x - b.d[k].tile0, nz, sm);
 }
 
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
@@ -264,9 +439,12 @@ int64_t sweep_rows_padded(int64_t nrow) {
 
 int sweep_ctas(int64_t nrow) { return (int)((nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps)); }
 
-int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, cudaStream_t stream) {
+int sweep_split_ctas(int64_t nrow) { return (int)((nrow + 63) / 64); }
+
+int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, bool split, cudaStream_t stream) {
   if (b.count == 0 || total_ctas == 0) return 0;
-  ef_sweep_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  if (split) ef_sweep_split_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  else ef_sweep_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
   note_launch();
   return 0;
 }
@@ -300,7 +478,7 @@ int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int
   SweepBatch b;
   b.count = 1;
   if (!sweep_desc(type, x, nrow, n, order, u_prep, dl, ml, work, codes, wcur, &b.d[0])) return 1;
-  return launch_ef_sweep_batch(b, sweep_ctas(nrow), stream);
+  return launch_ef_sweep_batch(b, sweep_ctas(nrow), false, stream);
 }
 
 // ---------------------------------------------------------------------------- no-allocation sweep

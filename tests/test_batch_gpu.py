@@ -34,7 +34,7 @@ def test_grouped_encode_matches_oracle(orc, many_rows):
     rng = np.random.default_rng(3)
     n = 256
     hess = {"a": _hessian(rng, n), "b": _hessian(rng, 512)}
-    rows = 1024 if many_rows else 40      # 20 x 1024 rows selects the one-warp sweep variant
+    rows = 1024 if many_rows else 40      # 20 x 1024 rows: several CTAs per tensor
     jobs = []
     for i in range(20 if many_rows else 6):
         tt = K_TYPES[i % 5]
@@ -144,3 +144,21 @@ def test_run_with_staged_weights_matches_resident():
     assert set(st_got) == set(st_want)
     for k in st_want:   # float64 sums reduced on the device in no fixed order
         assert st_got[k]["rel_err_vs_stock"] == pytest.approx(st_want[k]["rel_err_vs_stock"], rel=1e-9, abs=1e-12)
+
+
+def test_small_launch_long_rows_match_oracle(orc):
+    """A grouped launch too small to fill the GPU sends the rows of long tensors (n >= 2048)
+    to the column-split sweep (two warps per 32 rows); the bytes must still be the
+    reference's, ragged row counts included."""
+    rng = np.random.default_rng(17)
+    n = 2048
+    hess = {"a": _hessian(rng, n, T=4096)}
+    qw = np.diag(hess["a"]).astype(np.float32)
+    jobs = []
+    for i, (tt, rows) in enumerate((("Q2_K", 96), ("Q3_K", 33), ("Q6_K", 64), ("Q4_K", 1))):
+        W = (rng.standard_normal((rows, n)) * 0.02).astype(np.float32)
+        jobs.append((f"t{i}", tt, "EF", W, qw, "a", None))
+    got, _ = _encode(jobs, hess)
+    for name, tt, mode, W, qw_, hk, fw in jobs:
+        want, _ = orc.ef_encode(W, tt, qw_, hess[hk], n_iter=2, act_order=True)
+        assert np.array_equal(got[name], want), f"{name} {tt}: {np.count_nonzero(got[name] != want)} bytes differ"
