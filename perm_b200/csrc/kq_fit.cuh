@@ -257,6 +257,49 @@ __device__ __forceinline__ float fit_q3(const float (&x)[N], int nmax, float (&L
   return dead ? 0.0f : scale;
 }
 
+// The rest of make_qp_quants (kquant.py:205-235) once the inverse scale is chosen: codes, then
+// up to 5 coordinate-descent sweeps.  Codes are returned as the bytes numpy's astype(uint8)
+// gives (values wrap through int32).
+template <int N>
+__device__ __forceinline__ float fit_qp_tail(const float (&x)[N], const float (&w)[N], int nmax, float iscale,
+                                            bool dead, uint8_t (&Lout)[N]) {
+  float L[N];
+  Pw8 a, b;
+#pragma unroll
+  for (int i = 0; i < N; i++) L[i] = (float)min(nint(iscale * x[i]), nmax);
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    a.addi(i, w[i] * x[i] * L[i]);
+    b.addi(i, w[i] * L[i] * L[i]);
+  }
+  float sumlx = a.total(), suml2 = b.total();
+  bool active = !dead;
+#pragma unroll 1
+  for (int it = 0; it < 5 && active; it++) {
+    bool changed = false;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      const float wi = w[i], xi = x[i], Li = L[i];
+      const float slx = sumlx - wi * xi * Li;
+      const float sl2 = suml2 - wi * Li * Li;
+      const float den = (slx == 0.0f) ? 1.0f : slx;
+      const float nl = (float)min(nint(xi * sl2 / den), nmax);
+      const float slx2 = slx + wi * xi * nl;
+      const float sl22 = sl2 + wi * nl * nl;
+      const bool acc = slx > 0.0f && sl2 > 0.0f && nl != Li && slx2 * slx2 * suml2 > sumlx * sumlx * sl22;
+      L[i] = acc ? nl : Li;
+      sumlx = acc ? slx2 : sumlx;
+      suml2 = acc ? sl22 : suml2;
+      changed = changed || acc;
+    }
+    active = changed;
+  }
+  float d = (suml2 > 0.0f) ? sumlx / suml2 : 0.0f;
+#pragma unroll
+  for (int i = 0; i < N; i++) Lout[i] = dead ? (uint8_t)0 : (uint8_t)(int32_t)L[i];
+  return dead ? 0.0f : d;
+}
+
 // make_qp_quants (kquant.py:182-235): non-negative super-scale quantisation with 1 + 8
 // candidates and up to 5 coordinate-descent sweeps.  N is 16 or 8.  Codes are returned as
 // the bytes numpy's astype(uint8) gives (values wrap through int32).
@@ -298,41 +341,72 @@ __device__ __forceinline__ float fit_qp(const float (&x)[N], const float (&w)[N]
       iscale = isc;
     }
   }
-  float L[N];
-  Pw8 a, b;
+  return fit_qp_tail<N>(x, w, nmax, iscale, dead, Lout);
+}
+
+// Sum over an N-lane segment (N = 16 or 8) of one value per lane, in numpy's pairwise order
+// for N contiguous values with lane j as element j (Pw8: lane j < 8 adds lane j + 8, then
+// ((0+1)+(2+3))+((4+5)+(6+7)), then the +0 identity); every lane of the segment gets it.
+template <int N>
+__device__ __forceinline__ float seg_pw_sum(float v) {
+  if (N == 16) v = v + __shfl_down_sync(0xffffffffu, v, 8, 16);
+  v = v + __shfl_xor_sync(0xffffffffu, v, 1, N);
+  v = v + __shfl_xor_sync(0xffffffffu, v, 2, N);
+  v = v + __shfl_xor_sync(0xffffffffu, v, 4, N);
+  return __shfl_sync(0xffffffffu, 0.0f + v, 0, N);
+}
+
+// Maximum over an N-lane segment with np_max_step's NaN rule.  Equal values give the same
+// value in any order except for the sign of a zero maximum, which only ever meets the
+// dead-block test (max < 1e-15) and so cannot change a result.
+template <int N>
+__device__ __forceinline__ float seg_max(float v) {
 #pragma unroll
-  for (int i = 0; i < N; i++) L[i] = (float)min(nint(iscale * x[i]), nmax);
-#pragma unroll
-  for (int i = 0; i < N; i++) {
-    a.addi(i, w[i] * x[i] * L[i]);
-    b.addi(i, w[i] * L[i] * L[i]);
+  for (int o = 1; o < N; o <<= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o, N);
+    v = (v > u || v != v) ? v : u;
   }
-  float sumlx = a.total(), suml2 = b.total();
-  bool active = !dead;
-#pragma unroll 1
-  for (int it = 0; it < 5 && active; it++) {
-    bool changed = false;
-#pragma unroll
-    for (int i = 0; i < N; i++) {
-      const float wi = w[i], xi = x[i], Li = L[i];
-      const float slx = sumlx - wi * xi * Li;
-      const float sl2 = suml2 - wi * Li * Li;
-      const float den = (slx == 0.0f) ? 1.0f : slx;
-      const float nl = (float)min(nint(xi * sl2 / den), nmax);
-      const float slx2 = slx + wi * xi * nl;
-      const float sl22 = sl2 + wi * nl * nl;
-      const bool acc = slx > 0.0f && sl2 > 0.0f && nl != Li && slx2 * slx2 * suml2 > sumlx * sumlx * sl22;
-      L[i] = acc ? nl : Li;
-      sumlx = acc ? slx2 : sumlx;
-      suml2 = acc ? sl22 : suml2;
-      changed = changed || acc;
+  return v;
+}
+
+// make_qp_quants' scale search (kquant.py:182-204) for the two problems an N-lane segment
+// carries (the sub-block scales and the sub-block mins), one element per lane: lane j holds
+// element j of each (xa, xb) and its weight.  Each candidate's weighted error is reduced
+// across the segment in numpy's order, so the choice is the sequential fit's.  Returns each
+// problem's chosen inverse scale and dead flag, for fit_qp_tail.
+template <int N>
+__device__ __forceinline__ void fit_qp_search_lanes(float xa, float xb, float wme, int nmax, float& isc_a,
+                                                    bool& dead_a, float& isc_b, bool& dead_b) {
+  auto search = [&](float xv, float& isc_out, bool& dead_out) {
+    const float mx = seg_max<N>(xv);
+    const bool dead = mx < kGroupEps;
+    const float mxs = dead ? 1.0f : mx;
+    float iscale = (float)nmax / mxs;
+    float best;
+    {
+      const float scale = 1.0f / iscale;
+      const float l0 = (float)nint(iscale * xv);
+      const float d = xv - scale * l0;
+      best = seg_pw_sum<N>(wme * d * d);
     }
-    active = changed;
-  }
-  float d = (suml2 > 0.0f) ? sumlx / suml2 : 0.0f;
-#pragma unroll
-  for (int i = 0; i < N; i++) Lout[i] = dead ? (uint8_t)0 : (uint8_t)(int32_t)L[i];
-  return dead ? 0.0f : d;
+#pragma unroll 1
+    for (int s = -4; s <= 4; s++) {
+      if (s == 0) continue;
+      const float isc = (0.1f * (float)s + (float)nmax) / mxs;
+      const float sc = 1.0f / isc;
+      const float l = (float)min(nint(isc * xv), nmax);
+      const float d = xv - sc * l;
+      const float mse = seg_pw_sum<N>(wme * d * d);
+      if (mse < best && !dead) {
+        best = mse;
+        iscale = isc;
+      }
+    }
+    isc_out = iscale;
+    dead_out = dead;
+  };
+  search(xa, isc_a, dead_a);
+  search(xb, isc_b, dead_b);
 }
 
 }  // namespace cpk

@@ -140,7 +140,10 @@ __device__ __forceinline__ void q2k_encode_body(const float* __restrict__ x, con
       vw[j] = __shfl_sync(0xffffffffu, sw, j, 16);
     }
     uint8_t Lq[16];
-    const float dd = fit_qp<16>(vs, vw, 15, Lq);
+    float isa, isb;
+    bool da, db;
+    fit_qp_search_lanes<16>(scale, negmin, sw, 15, isa, da, isb, db);
+    const float dd = fit_qp_tail<16>(vs, vw, 15, sub == 1 ? isb : isa, sub == 1 ? db : da, Lq);
     uint32_t words[4];
     pack_bytes(Lq, words);
     uint32_t ws[4], wm[4];
@@ -423,7 +426,10 @@ __device__ __forceinline__ void q45k_encode_body(const float* __restrict__ x, co
       vw[j] = __shfl_sync(0xffffffffu, sw, j, 8);
     }
     uint8_t Lq[8];
-    const float dd = fit_qp<8>(vs, vw, 63, Lq);
+    float isa, isb;
+    bool da, db;
+    fit_qp_search_lanes<8>(scale, negmin, sw, 63, isa, da, isb, db);
+    const float dd = fit_qp_tail<8>(vs, vw, 63, sub == 1 ? isb : isa, sub == 1 ? db : da, Lq);
     uint32_t words[4];
     pack_bytes(Lq, words);
     uint32_t ws[4], wm[4];
