@@ -117,28 +117,38 @@ __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_consta
   for (int p = 0; p < 4; p++) {
     const int c0 = 16 * p;
     if (warp == 0) {
+      // the 16 x 16 diagonal block in registers: lane r (and r + 16) holds row r; the pivot and
+      // column c's values come by shuffle, so a column step has no shared-memory round trip
+      const int r = lane & 15;
+      double lr[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) lr[k] = a[c0 + r][c0 + k];  // zero above the diagonal
+      bool okp = true;
+#pragma unroll
       for (int c = 0; c < 16; c++) {
-        const double d = a[c0 + c][c0 + c];
-        if (!(d > 0.0)) {  // uniform: every lane read the same pivot
-          if (lane == 0) bad = 1;
-          break;
-        }
+        const double d = __shfl_sync(0xffffffffu, lr[c], c);
+        okp = okp && (d > 0.0);  // uniform: every lane got the same pivot
+        if (!okp) continue;      // (no break: the loop must unroll to keep lr in registers)
         const double sq = sqrt(d), is = rsqrt(d);
-        __syncwarp();
-        if (lane > c && lane < 16) a[c0 + lane][c0 + c] *= is;
-        if (lane == 0) {
-          a[c0 + c][c0 + c] = sq;
-          isq[c0 + c] = is;
+        if (r == c) {
+          lr[c] = sq;
+          if (lane == c) isq[c0 + c] = is;
+        } else if (r > c) {
+          lr[c] *= is;
         }
-        __syncwarp();
-        const int r = lane & 15;  // row r, columns c + 1 + (lane >> 4) + 2i up to the diagonal
-        if (r > c) {
-          const double lrc = a[c0 + r][c0 + c];
-          for (int kk = c + 1 + (lane >> 4); kk <= r; kk += 2) a[c0 + r][c0 + kk] -= lrc * a[c0 + kk][c0 + c];
+#pragma unroll
+        for (int k = c + 1; k < 16; k++) {
+          const double lkc = __shfl_sync(0xffffffffu, lr[c], k);
+          if (r >= k) lr[k] = fma(-lr[c], lkc, lr[k]);
         }
-        __syncwarp();
       }
-      __syncwarp();  // lane 0's bad flag
+      if (!okp) {
+        if (lane == 0) bad = 1;
+      } else if (lane < 16) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[c0 + r][c0 + k] = lr[k];
+      }
+      __syncwarp();  // the factor and lane 0's bad flag
       if (!bad && lane < 16) {  // inverse of the 16 x 16 factor into x's diagonal block
         const int j = lane;
         double col[16];
