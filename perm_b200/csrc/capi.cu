@@ -408,10 +408,10 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
   cudaStream_t s = (cudaStream_t)stream;
   static thread_local cpk::SweepBatch b;
-  // A launch too small to keep the GPU busy (under two waves of four resident 128-row CTAs per
-  // SM) is bounded by its longest rows, whose columns one lane walks serially; such a launch
-  // runs the column-split form, two warps per 32 rows, each applying the errors to half of
-  // every block.
+  // A launch too small to keep the GPU busy is bounded by its longest rows, whose columns one
+  // lane walks serially; such a launch runs the column-split form, several warps per 32 rows,
+  // each applying the errors to its share of every block: four warps under one and a half
+  // waves of four resident 128-row CTAs per SM, two under two waves (measured crossovers).
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;
@@ -422,14 +422,14 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   int64_t plain = 0;
   for (int i = 0; i < count; i++)
     if (jobs[i].nrow > 0) plain += cpk::sweep_ctas(jobs[i].nrow);
-  const bool small_launch = plain < 2LL * 4 * sms;
+  const int split = plain < 6LL * sms ? 4 : plain < 8LL * sms ? 2 : 1;
   b.count = 0;
   int tiles = 0;
   for (int i = 0; i <= count; i++) {
     const bool flush = (i == count) || b.count == cpk::kSweepBatchMax;
     if (flush && b.count) {
       ProfScope ps(kProfSweep, s);
-      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, small_launch, s), "cp_ef_sweep_batch"))
+      if (int rc = check_rc(cpk::launch_ef_sweep_batch(b, tiles, split, s), "cp_ef_sweep_batch"))
         return rc;
       b.count = 0;
       tiles = 0;
@@ -451,7 +451,7 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
     if (j.pitch > (int64_t)1 << 31) return set_err(CP_ERR_SHAPE, "cp_ef_sweep_batch: pitch too large");
     d.pitch = (int)j.pitch;
     d.tile0 = tiles;
-    tiles += small_launch ? cpk::sweep_split_ctas(j.nrow) : cpk::sweep_ctas(j.nrow);
+    tiles += split > 1 ? cpk::sweep_split_ctas(j.nrow, split) : cpk::sweep_ctas(j.nrow);
     b.count++;
   }
   return CP_OK;

@@ -33,10 +33,11 @@ bool sweep_desc(int type, const float* x, int64_t nrow, int64_t n, const int* or
 // Rows a tensor's sweep CTAs cover (nrow rounded up to 32 * kSweepWarps): the smallest pitch.
 int64_t sweep_rows_padded(int64_t nrow);
 int sweep_ctas(int64_t nrow);
-// CTAs of the column-split form (64 rows each, two warps per 32 rows, each applying the
-// errors to half of every 64-column block): for launches too small to fill the GPU.
-int sweep_split_ctas(int64_t nrow);
-int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, bool split, cudaStream_t stream);
+// CTAs of the column-split form with `split` (2 or 4) warps per 32 rows, each applying the
+// errors to 1/split of every 64-column block: for launches too small to fill the GPU.
+int sweep_split_ctas(int64_t nrow, int split);
+// split: 1 for the ordinary form (sweep_ctas CTAs), 2 or 4 for the column-split form.
+int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, int split, cudaStream_t stream);
 // Sweep with its working rows in a fixed per-device array (no caller workspace).
 constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
 int launch_ef_sweep_noalloc(int type, const float* x, int64_t nrow, int64_t n, const int* order, const float* u_prep,

@@ -76,8 +76,8 @@ struct SweepSmem {
   union __align__(16) {
     float re[kSwST][kSweepWarps][kSwJS][32];         // ring: errors e_jj of each warp's rows
     struct {                                         // column-split form (sweep_rows_split)
-      float re[kSwST][2][kSwJS][32];                 // ring: errors e_jj of the CTA's two row tiles
-      float xb[2][32][32];                           // errors of block columns 0..31, per row tile
+      float re[kSwST][2][kSwJS][32];                 // ring: errors e_jj of the CTA's row tiles
+      float xb[2 * 32 * 32];                         // errors handed between a tile's warps
     } cs;
   };
 };
@@ -225,26 +225,30 @@ __device__ __forceinline__ void sweep_rows(const SweepDesc& t, int cta, float nz
   }
 }
 
-// Column-split form, for long rows in launches too small to fill the GPU: a CTA of four warps
-// owns 64 rows; warps 2p and 2p + 1 share rows 32p .. 32p + 31 (lane = row) and split every
-// 64-column block, warp h keeping block columns 32h .. 32h + 31 in registers.  Each warp
-// applies the earlier columns' errors to its half only, which halves the serial work of a
-// row.  In the panel, warp 0 of the pair quantizes columns 0..31 and hands their errors to
-// warp 1 through shared memory; warp 1 applies them in ascending order and then quantizes
-// columns 32..63.  Every element still receives exactly the reference's updates in the
-// reference's order, each rounded as the reference rounds it.
+// Column-split form, for launches too small to fill the GPU (their time is the serial work of
+// their longest rows): S = 2 or 4 warps share each 32-row tile (lane = row), warp h keeping
+// block columns CW*h .. CW*h + CW - 1 (CW = 64 / S) of every 64-column block in registers, so
+// each warp applies the earlier columns' errors to 1/S of the row.  The panel goes warp by
+// warp: warp q quantizes its columns and leaves their errors in shared memory; after a
+// barrier the warps after it apply them, in ascending order, to their own columns.  Every
+// element still receives exactly the reference's updates in the reference's order, each
+// rounded as the reference rounds it.
+template <int S>
 __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, float nz, SweepSmem& sm) {
+  constexpr int G = kSweepWarps / S;  // row tiles per CTA
+  constexpr int CW = kSwB / S;        // block columns per warp
+  constexpr int NSP = CW / 16;        // 16-column sub-panels per warp
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int pair = warp >> 1, h = warp & 1, cb = 32 * h;
+  const int grp = warp / S, h = warp % S, cb = CW * h;
   const int n = t.n, nrow = t.nrow;
-  const int tile32 = cta * 2 + pair;
+  const int tile32 = cta * G + grp;
   const int row = tile32 * 32 + lane;
   const bool rv = row < nrow;
   const int sbw = t.sbw, lo = t.lo, hi = t.hi, nsub = n / sbw;
   const float* __restrict__ U = t.u;
   const float* __restrict__ diagU = t.u + (size_t)n * n;
   float* __restrict__ E = t.work;                              // [tile32][n][32]
-  const float* __restrict__ Ecta = t.work + (size_t)cta * 2 * n * 32;
+  const float* __restrict__ Ecta = t.work + (size_t)cta * G * n * 32;
   float* __restrict__ Erow = E + (size_t)tile32 * n * 32 + lane;
   const int64_t cs = t.pitch ? t.pitch : 1, rs = t.pitch ? 1 : n, rsg = t.pitch ? 1 : nsub;
   const float* __restrict__ xr = t.x + (size_t)(rv ? row : 0) * rs;
@@ -252,16 +256,18 @@ __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, fl
   const float* __restrict__ mlr = t.ml ? t.ml + (size_t)(rv ? row : 0) * rsg : nullptr;
   int8_t* __restrict__ codes = t.codes + (size_t)row * rs;
   float* __restrict__ wout = t.wout ? t.wout + (size_t)row * rs : nullptr;
+  // errors handed between the warps of a tile: block columns 0 .. 64 - CW - 1
+  float* __restrict__ xb = sm.cs.xb + (size_t)grp * (kSwB - CW) * 32 + lane;
 
   for (int j0 = 0; j0 < n; j0 += kSwB) {
     __syncthreads();  // the previous block's readers of the shared buffers are done
     const int nst = j0 / kSwJS;
     // stage s = U rows jj in [s*JS, s*JS + JS) of this block's columns + the errors of those
-    // jj for the CTA's two row tiles (16 + 2 * 8 = 32 chunks of 16 bytes per jj)
+    // jj for the CTA's G row tiles (16 + 8 G chunks of 16 bytes per jj)
     auto issue = [&](int s) {
       if (s < nst) {
         const int st = s % kSwST, jj0 = s * kSwJS;
-        for (int c = tid; c < kSwJS * (16 + 8 * 2); c += kSwThreads) {
+        for (int c = tid; c < kSwJS * (16 + 8 * G); c += kSwThreads) {
           if (c < kSwJS * 16) {
             const int k = c >> 4, c4 = c & 15;
             cp_async16(&sm.ru[st][k][4 * c4], U + (size_t)(jj0 + k) * n + j0 + 4 * c4);
@@ -287,12 +293,12 @@ __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, fl
     }
     __syncthreads();
 
-    // 1. this warp's half of the block, w = x[row, order[j0 + cb + c]]
-    float w[32];
+    // 1. this warp's columns of the block, w = x[row, order[j0 + cb + c]]
+    float w[CW];
 #pragma unroll
-    for (int c = 0; c < 32; c++) w[c] = rv ? __ldg(xr + sm.ord[cb + c] * cs) : 0.0f;
+    for (int c = 0; c < CW; c++) w[c] = rv ? __ldg(xr + sm.ord[cb + c] * cs) : 0.0f;
 
-    // 2. errors of every earlier column, ascending jj, on this warp's 32 columns
+    // 2. errors of every earlier column, ascending jj, on this warp's columns
     for (int s = 0; s < nst; s++) {
       cp_async_wait<kSwST - 2>();
       __syncthreads();  // stage s landed for everyone; everyone is done with stage s - 1
@@ -300,10 +306,10 @@ __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, fl
       const int st = s % kSwST;
 #pragma unroll
       for (int k = 0; k < kSwJS; k++) {
-        const float e = sm.cs.re[st][pair][k][lane];
+        const float e = sm.cs.re[st][grp][k][lane];
         const float4* u4 = reinterpret_cast<const float4*>(&sm.ru[st][k][cb]);
 #pragma unroll
-        for (int c4 = 0; c4 < 8; c4++) {
+        for (int c4 = 0; c4 < CW / 4; c4++) {
           const float4 u = u4[c4];
           upd2(w[4 * c4], w[4 * c4 + 1], e, e, u.x, u.y, nz);
           upd2(w[4 * c4 + 2], w[4 * c4 + 3], e, e, u.z, u.w, nz);
@@ -312,11 +318,11 @@ __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, fl
     }
     cp_async_wait<0>();
 
-    // 3. panel of this warp's half: two sub-panels of 16 (as in sweep_rows, with the later
-    // group of the half updated after the first); warp 0 also leaves its errors in xb
+    // 3. panel of this warp's columns: NSP sub-panels of 16 (as in sweep_rows, the later
+    // sub-panel of the warp updated after the first); the errors go to xb for later warps
     auto panel = [&]() {
 #pragma unroll 1
-      for (int p = 0; p < 2; p++) {
+      for (int p = 0; p < NSP; p++) {
         const int a0 = cb + 16 * p;
         float es[16];
         float cd[16], cm[16];
@@ -342,41 +348,42 @@ __device__ __forceinline__ void sweep_rows_split(const SweepDesc& t, int cta, fl
             if (wout) wout[j * cs] = wa;
           }
           Erow[(size_t)(j0 + a) * 32] = e;
-          if (h == 0) sm.cs.xb[pair][a][lane] = e;
+          if (h < S - 1) xb[a * 32] = e;
           es[i] = e;
 #pragma unroll
           for (int b = i + 1; b < 16; b++) w[b] = w[b] - e * sm.ud[a][a0 + b];
         }
-        if (p == 0) {  // the half's second 16 columns (w[16..31])
+        if (NSP == 2 && p == 0) {  // the warp's second 16 columns (w[16..31])
 #pragma unroll
           for (int i = 0; i < 16; i++) {
             const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[a0 + i][a0 + 16]);
 #pragma unroll
             for (int c2 = 0; c2 < 8; c2++) {
               const float2 u = u2[c2];
-              upd2(w[16 + 2 * c2], w[16 + 2 * c2 + 1], es[i], es[i], u.x, u.y, nz);
+              upd2(w[(16 + 2 * c2) % CW], w[(16 + 2 * c2 + 1) % CW], es[i], es[i], u.x, u.y, nz);
             }
           }
 #pragma unroll
-          for (int c = 0; c < 16; c++) w[c] = w[c + 16];
+          for (int c = 0; c < CW - 16; c++) w[c] = w[c + 16];
         }
       }
     };
-    if (h == 0) panel();
-    __syncthreads();  // warp 0's errors of columns 0..31 are in xb
-    if (h == 1) {
-      // the errors of block columns 0..31, ascending, on columns 32..63
-#pragma unroll 4
-      for (int i = 0; i < 32; i++) {
-        const float e = sm.cs.xb[pair][i][lane];
-        const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[i][32]);
 #pragma unroll
-        for (int c2 = 0; c2 < 16; c2++) {
-          const float2 u = u2[c2];
-          upd2(w[2 * c2], w[2 * c2 + 1], e, e, u.x, u.y, nz);
+    for (int q = 0; q < S; q++) {
+      if (h == q) panel();
+      __syncthreads();  // warp q's errors are in xb
+      if (h > q) {      // ... applied, ascending, to this warp's columns
+#pragma unroll 4
+        for (int i = 0; i < CW; i++) {
+          const float e = xb[(CW * q + i) * 32];
+          const float2* u2 = reinterpret_cast<const float2*>(&sm.ud[CW * q + i][cb]);
+#pragma unroll
+          for (int c2 = 0; c2 < CW / 2; c2++) {
+            const float2 u = u2[c2];
+            upd2(w[2 * c2], w[2 * c2 + 1], e, e, u.x, u.y, nz);
+          }
         }
       }
-      panel();
     }
   }
 }
@@ -397,13 +404,14 @@ __global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_batch_kernel(const __g
   sweep_rows(b.d[k], blockIdx.x - b.d[k].tile0, nz, sm);
 }
 
-// The column-split form as its own kernel, so that neither form's register allocation
-// constrains the other.
+// The column-split forms as kernels of their own, so that no form's register allocation
+// constrains another's.
+template <int S>
 __global__ void __launch_bounds__(kSwThreads, 4) ef_sweep_split_batch_kernel(const __grid_constant__ SweepBatch b,
                                                                              float nz) {
   __shared__ SweepSmem sm;
   const int k = sweep_desc_of(b, blockIdx.x);
-  sweep_rows_split(b.d[k], blockIdx.x - b.d[k].tile0, nz, sm);
+  sweep_rows_split<S>(b.d[k], blockIdx.x - b.d[k].tile0, nz, sm);
 }
 
 size_t ef_sweep_workspace_bytes(int64_t nrow, int64_t n) {
@@ -439,12 +447,17 @@ int64_t sweep_rows_padded(int64_t nrow) {
 
 int sweep_ctas(int64_t nrow) { return (int)((nrow + 32 * kSweepWarps - 1) / (32 * kSweepWarps)); }
 
-int sweep_split_ctas(int64_t nrow) { return (int)((nrow + 63) / 64); }
+int sweep_split_ctas(int64_t nrow, int split) {
+  const int rows = 32 * (kSweepWarps / split);
+  return (int)((nrow + rows - 1) / rows);
+}
 
-int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, bool split, cudaStream_t stream) {
+int launch_ef_sweep_batch(const SweepBatch& b, int total_ctas, int split, cudaStream_t stream) {
   if (b.count == 0 || total_ctas == 0) return 0;
-  if (split) ef_sweep_split_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
-  else ef_sweep_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  if (split == 4) ef_sweep_split_batch_kernel<4><<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  else if (split == 2) ef_sweep_split_batch_kernel<2><<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  else if (split == 1) ef_sweep_batch_kernel<<<total_ctas, kSwThreads, 0, stream>>>(b, -0.0f);
+  else return 2;
   note_launch();
   return 0;
 }
@@ -478,7 +491,7 @@ int launch_ef_sweep(int type, const float* x, int64_t nrow, int64_t n, const int
   SweepBatch b;
   b.count = 1;
   if (!sweep_desc(type, x, nrow, n, order, u_prep, dl, ml, work, codes, wcur, &b.d[0])) return 1;
-  return launch_ef_sweep_batch(b, sweep_ctas(nrow), false, stream);
+  return launch_ef_sweep_batch(b, sweep_ctas(nrow), 1, stream);
 }
 
 // ---------------------------------------------------------------------------- no-allocation sweep

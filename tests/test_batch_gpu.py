@@ -162,3 +162,22 @@ def test_small_launch_long_rows_match_oracle(orc):
     for name, tt, mode, W, qw_, hk, fw in jobs:
         want, _ = orc.ef_encode(W, tt, qw_, hess[hk], n_iter=2, act_order=True)
         assert np.array_equal(got[name], want), f"{name} {tt}: {np.count_nonzero(got[name] != want)} bytes differ"
+
+
+def test_medium_launch_matches_oracle(orc):
+    """A grouped launch of one and a half to two waves of ordinary sweep CTAs runs the
+    two-warp column split (smaller launches take the four-warp one); the bytes must be the
+    reference's."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rng = np.random.default_rng(23)
+    hess = {"a": _hessian(rng, 256), "b": _hessian(rng, 512)}
+    rows = 7 * sms * 128 - 77            # about 7 * sms ordinary 128-row CTAs: 1.75 waves of 4 per SM
+    jobs = [("big", "Q2_K", "EF", (rng.standard_normal((rows, 256)) * 0.02).astype(np.float32),
+             np.diag(hess["a"]).astype(np.float32), "a", None),
+            ("small", "Q3_K", "EF", (rng.standard_normal((45, 512)) * 0.02).astype(np.float32),
+             np.diag(hess["b"]).astype(np.float32), "b", None)]
+    got, _ = _encode(jobs, hess, stats=False)
+    for name, tt, mode, W, qw, hk, fw in jobs:
+        want, _ = orc.ef_encode(W, tt, qw, hess[hk], n_iter=2, act_order=True)
+        assert np.array_equal(got[name], want), f"{name} {tt}: {np.count_nonzero(got[name] != want)} bytes differ"
