@@ -1,5 +1,5 @@
 """Small, fixed micro-cases of the encoder's kernels, for timing and for profiler captures
-(`ncu ... python -m perm_b200.bench_cases <case>`).  Each case holds at most a few hundred MB
+(`ncu ... python bench_cases.py <case>`).  Each case holds at most a few hundred MB
 on the device and runs its kernels a few times.
 
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
@@ -11,10 +11,15 @@ on the device and runs its kernels a few times.
     xtx      X^T X of 32768 bf16 tokens at d = 1024, 2048, 3072 (tcgen05 kernel)
     xtx_f32  the same with float32 tokens (hi/lo bf16 split, four products)
 """
+import os
 import sys
 import time
 
 import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
 
 
 def _hess(torch, n, seed, T=4096):
@@ -26,8 +31,8 @@ def _hess(torch, n, seed, T=4096):
 
 
 def _sweep_case(torch, reps, shapes):
-    from . import _native as nat
-    from .encoder import Encoder, Job
+    from perm_b200 import _native as nat
+    from perm_b200.encoder import Encoder, Job
     hs, jobs = {}, []
     for i, (nrow, n, tt, hk) in enumerate(shapes):
         if hk not in hs:
@@ -85,7 +90,7 @@ def case_sweep_layers(torch, reps):
 
 
 def case_fit(torch, reps):
-    from . import kquant as kq
+    from perm_b200 import kquant as kq
     x = torch.randn(4096, 4096, device="cuda") * 0.02
     qw = torch.exp(torch.randn(4096, device="cuda"))
     out = kq.quantize_dev("Q2_K", x, qw)
@@ -101,7 +106,7 @@ def case_fit(torch, reps):
 
 
 def case_factor(torch, reps):
-    from .encoder import Encoder
+    from perm_b200.encoder import Encoder
     hs = {f"a{i}": _hess(torch, 1024, i) for i in range(16)}
     hs.update({f"b{i}": _hess(torch, 3072, 100 + i) for i in range(4)})
     ds = {k: torch.diagonal(v).cpu().numpy() for k, v in hs.items()}
@@ -127,7 +132,7 @@ def _xtx_tile_flops(T, d):
 def case_factor_model(torch, reps):
     """The whole Qwen3-0.6B-shaped model's 112 factorisations (56 at n = 1024, 28 at 2048,
     28 at 3072) through Encoder.factor, wall time with a device sync."""
-    from .encoder import Encoder
+    from perm_b200.encoder import Encoder
     base = {1024: _hess(torch, 1024, 1), 2048: _hess(torch, 2048, 2), 3072: _hess(torch, 3072, 3)}
     hs = {}
     for l in range(28):
@@ -147,7 +152,7 @@ def case_factor_model(torch, reps):
 
 
 def case_xtx(torch, reps, dtype="bf16"):
-    from . import hessians
+    from perm_b200 import hessians
     out = []
     T = 32768
     for d in (1024, 2048, 3072):

@@ -84,7 +84,19 @@ int cp_kquant_repack(int ggml_type, uint8_t* raw, const int8_t* codes, int64_t n
 int cp_weighted_err(int ggml_type, const uint8_t* raw, const float* x, const float* w, int64_t nrow, int64_t n,
                     double* out, void* stream);
 
-/* hessians.py:542-560 load_hessian arithmetic: H (float64 [d, d]) = float64(h16) * hscale with
+/* perm/objective.py:22-28 (x[idx] row sample, then x[:, perm]): out float32 [nrow_out, n_out]
+ * with out[i][j] = x[row(i) * ld + col(j)], row(i) = rows[i] and col(j) = cols[j] (int64 device
+ * arrays), or i and j where rows / cols is NULL.  Indices are not range-checked. */
+int cp_gather_f32(const float* x, int64_t ld, const int64_t* rows, int64_t nrow_out, const int64_t* cols,
+                  int64_t n_out, float* out, void* stream);
+
+/* perm/objective.py:32-33 and 42-49: out float64 [n] with out[c] = sum over r < nrow of
+ * (x[r * ld + c] - y[r * ld + c])^2 (y == NULL: x^2), accumulated in float64 in a fixed order
+ * (repeated calls give identical bits; the reference's own summation order differs, so the
+ * last bits of float64 may too). */
+int cp_col_sqdiff(const float* x, const float* y, int64_t nrow, int64_t n, int64_t ld, double* out, void* stream);
+
+/* hessians.py:225-245 load_hessian arithmetic: H (float64 [d, d]) = float64(h16) * hscale with
  * the exact float32 diagonal diag32 (may be NULL) written over it; h16 holds float16 bits. */
 int cp_hessian_decode(const uint16_t* h16, const float* diag32, double hscale, int64_t d, double* H, void* stream);
 
@@ -136,8 +148,10 @@ int cp_ef_sweep(int ggml_type, const float* x, int64_t nrow, int64_t n, const in
  * library, held on every GPU that loads it until the process exits; this call itself
  * allocates nothing.  Shapes with ceil(nrow/128)*128 * n * 4 > CP_NOALLOC_SCRATCH_BYTES are
  * rejected with CP_ERR_WORKSPACE.  The first call on a device looks the array's address up
- * (make that call before any stream capture).  All calls share the array: calls that
- * overlap on the GPU (other streams, other threads) race and must be serialised. */
+ * (make that call before any stream capture) and keeps it for the life of the process, so
+ * the call must not be used on a device after cudaDeviceReset (or any other teardown of its
+ * primary context) in the same process.  All calls share the array: calls that overlap on
+ * the GPU (other streams, other threads) race and must be serialised. */
 #define CP_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 int cp_ef_sweep_noalloc(int ggml_type, const float* x, int64_t nrow, int64_t n, const int32_t* order,
                         const float* u_prepared, const float* dl, const float* ml, int8_t* codes, float* w_out,
@@ -236,7 +250,7 @@ int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream);
  * input, the hi/lo bf16 copies of x.  Zero-fill it once when it is allocated. */
 size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d);
 
-/* hessians.py:455-470 hook arithmetic (`x.float(); acc += x.T @ x`): H += x^T x for x
+/* hessians.py:137-152 hook arithmetic (`x.float(); acc += x.T @ x`): H += x^T x for x
  * [T, d] row-major (bf16, or float32 split exactly into hi + lo bf16 with a 2^-17 relative
  * remainder), H float32 [d, d] row-major, d a multiple of 8, accumulated in float32 on the
  * tensor cores.  H stays exactly symmetric and repeated calls give identical bits.  One

@@ -113,6 +113,8 @@ def lib():
         "cp_ef_sweep_rows": ([I64], I64),
         "cp_transpose_batch": ([P, I, P], I),
         "cp_fetch_host": ([P, P, I64, P], I),
+        "cp_gather_f32": ([P, I64, P, I64, P, I64, P, P], I),
+        "cp_col_sqdiff": ([P, P, I64, I64, I64, P, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

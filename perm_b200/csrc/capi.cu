@@ -11,6 +11,9 @@
 #include "xtx_kernels.h"
 #include "layout_kernels.h"
 
+static_assert(cpk::kNoAllocScratchBytes == CP_NOALLOC_SCRATCH_BYTES,
+              "the public no-allocation limit must equal the scratch array's size");
+
 namespace {
 
 thread_local char g_err[512] = "";
@@ -254,14 +257,21 @@ int cp_ef_sweep_noalloc(int t, const float* x, int64_t nrow, int64_t n, const in
   cpk::grid_spec(t, &sbw, &lo, &hi, &hm);
   if (!x || !order || !ut2 || !dl || (hm && !ml) || !codes) return set_err(CP_ERR_ARG, "null pointer");
   if (cpk::ef_sweep_workspace_bytes(nrow, n) > cpk::kNoAllocScratchBytes) {
+    const int pad = 32 * cpk::kSweepWarps;
     std::snprintf(g_err, sizeof(g_err),
-                  "cp_ef_sweep_noalloc: ceil(nrow/32)*32 * n * 4 bytes = %zu exceeds the fixed %zu-byte scratch; "
+                  "cp_ef_sweep_noalloc: ceil(nrow/%d)*%d * n * 4 bytes = %zu exceeds the fixed %zu-byte scratch; "
                   "use cp_ef_sweep with a workspace",
-                  cpk::ef_sweep_workspace_bytes(nrow, n), cpk::kNoAllocScratchBytes);
+                  pad, pad, cpk::ef_sweep_workspace_bytes(nrow, n), cpk::kNoAllocScratchBytes);
     return CP_ERR_WORKSPACE;
   }
   const int rc = cpk::launch_ef_sweep_noalloc(t, x, nrow, n, order, ut2, dl, ml, codes, w_out, (cudaStream_t)stream);
-  if (rc == 4) return check_launch("cp_ef_sweep_noalloc: locating the fixed scratch");
+  if (rc == 4) {
+    // a failed CUDA call leaves its error pending; a lookup that "succeeded" with a null
+    // address leaves none, and must not be reported as a sweep that ran
+    if (check_launch("cp_ef_sweep_noalloc: locating the fixed scratch") == CP_OK)
+      return set_err(CP_ERR_CUDA, "cp_ef_sweep_noalloc: the fixed scratch has no device address on this device");
+    return CP_ERR_CUDA;
+  }
   if (rc == 5) return set_err(CP_ERR_ARG, "cp_ef_sweep_noalloc: device index out of range");
   return check_rc(rc, "cp_ef_sweep_noalloc");
 }
@@ -412,13 +422,7 @@ int cp_ef_sweep_batch(const cp_sweep_job* jobs, int count, void* stream) {
   // lane walks serially; such a launch runs the column-split form, several warps per 32 rows,
   // each applying the errors to its share of every block: four warps under one and a half
   // waves of four resident 128-row CTAs per SM, two under two waves (measured crossovers).
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
-                                                  cudaSuccess || sms <= 0)
-      sms = 148;
-  }
+  const int sms = cpk::device_sm_count();
   int64_t plain = 0;
   for (int i = 0; i < count; i++)
     if (jobs[i].nrow > 0) plain += cpk::sweep_ctas(jobs[i].nrow);
@@ -510,6 +514,25 @@ int cp_fetch_host(void* dst, const void* src_host, int64_t bytes, void* stream) 
   return check_rc(cpk::launch_fetch_host(dst, mapped, bytes, (cudaStream_t)stream), "cp_fetch_host");
 }
 
+int cp_gather_f32(const float* x, int64_t ld, const int64_t* rows, int64_t nrow_out, const int64_t* cols,
+                  int64_t n_out, float* out, void* stream) {
+  if (nrow_out < 0 || n_out < 0 || ld < 0) return set_err(CP_ERR_SHAPE, "cp_gather_f32: negative size");
+  if (nrow_out == 0 || n_out == 0) return CP_OK;
+  if (!x || !out) return set_err(CP_ERR_ARG, "null pointer");
+  if (!cols && ld < n_out) return set_err(CP_ERR_SHAPE, "cp_gather_f32: ld smaller than the row");
+  ProfScope ps(kProfOther, (cudaStream_t)stream);
+  return check_rc(cpk::launch_gather_f32(x, ld, rows, nrow_out, cols, n_out, out, (cudaStream_t)stream),
+                  "cp_gather_f32");
+}
+
+int cp_col_sqdiff(const float* x, const float* y, int64_t nrow, int64_t n, int64_t ld, double* out, void* stream) {
+  if (nrow < 0 || n < 0 || ld < n) return set_err(CP_ERR_SHAPE, "cp_col_sqdiff: bad nrow, n or ld");
+  if (n == 0) return CP_OK;
+  if (!x || !out) return set_err(CP_ERR_ARG, "null pointer");
+  ProfScope ps(kProfOther, (cudaStream_t)stream);
+  return check_rc(cpk::launch_col_sqdiff(x, y, nrow, n, ld, out, (cudaStream_t)stream), "cp_col_sqdiff");
+}
+
 int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream) {
   if (count < 0 || (count > 0 && !jobs)) return set_err(CP_ERR_ARG, "bad job list");
   cudaStream_t s = (cudaStream_t)stream;
@@ -544,15 +567,10 @@ int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream) {
   return CP_OK;
 }
 
-static int num_sms_current() {
-  int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
 
 size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d) {
   if (T < 0 || d <= 0 || (dtype != CP_XTX_BF16 && dtype != CP_XTX_F32)) return 0;
-  return cpk::xtx_plan(T, d, dtype == CP_XTX_F32, num_sms_current()).ws_bytes;
+  return cpk::xtx_plan(T, d, dtype == CP_XTX_F32, cpk::device_sm_count()).ws_bytes;
 }
 
 int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, void* workspace, size_t ws_bytes,
@@ -564,7 +582,7 @@ int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, 
   if (!x || !H || !workspace) return set_err(CP_ERR_ARG, "null pointer");
   if (((uintptr_t)x | (uintptr_t)H | (uintptr_t)workspace) & 15)
     return set_err(CP_ERR_ARG, "x, H and workspace must be 16-byte aligned");
-  const cpk::XtxPlan p = cpk::xtx_plan(T, d, dtype == CP_XTX_F32, num_sms_current());
+  const cpk::XtxPlan p = cpk::xtx_plan(T, d, dtype == CP_XTX_F32, cpk::device_sm_count());
   if (ws_bytes < p.ws_bytes) return set_err(CP_ERR_WORKSPACE, "workspace smaller than cp_xtx_workspace_bytes()");
   cudaStream_t s = (cudaStream_t)stream;
   ProfScope ps(kProfOther, s);

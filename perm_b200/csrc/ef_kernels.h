@@ -1,10 +1,24 @@
 // Internal launcher declarations for the error-feedback path (sweep, U layout, factorisation).
 #pragma once
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 namespace cpk {
+// Streaming multiprocessors of the current device, looked up once per device index (148 on
+// B200; 148 is also the answer when the lookup fails).  Safe to call from several threads.
+inline int device_sm_count() {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+  cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
 // Rows per sweep CTA = 32 * kSweepWarps.
 constexpr int kSweepWarps = 4;
 // One tensor of a grouped error-feedback sweep launch (CTAs [tile0, tile0 + sweep_ctas(nrow))).

@@ -510,7 +510,8 @@ void* g_noalloc_addr[kMaxNoAllocDevices] = {};
 }  // namespace
 
 // Device address of the scratch array on the current device; looked up on the first call per
-// device (which must therefore not happen during a stream capture).
+// device (which must therefore not happen during a stream capture) and kept until the process
+// exits: a device reset would leave the cached address stale, which the header rules out.
 static int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 4;

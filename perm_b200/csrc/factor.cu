@@ -30,12 +30,7 @@ __host__ __device__ inline int kchunk(int K, int S) { return ((K + S - 1) / S + 
 // GPU short of one wave (3 resident 128-thread tile CTAs per SM), then as little as fills it.
 // Every extra split costs a partial-tile write and a reduction pass.
 static int ksplit_batch(int K, int tiles, int count) {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-  }
+  const int sms = device_sm_count();
   const int smax = ksplit(K);
   const long long base = (long long)tiles * count, slots = 3LL * sms;
   if (smax <= 1 || base >= slots) return 1;

@@ -454,7 +454,7 @@ int launch_repack(int type, uint8_t* raw, const int8_t* codes, int64_t nrow, int
   return 0;
 }
 
-// hessians.py:542-560 load_hessian: H = float64(H16) * hscale, then the exact float32
+// hessians.py:225-245 load_hessian: H = float64(H16) * hscale, then the exact float32
 // diagonal written over it (diag32 may be null for the old float32-only layout).
 __global__ void hessian_decode_kernel(const uint16_t* __restrict__ h16, const float* __restrict__ diag32, double hscale,
                                       int64_t d, double* __restrict__ H) {

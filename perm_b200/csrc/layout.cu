@@ -137,4 +137,85 @@ int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles
   return 0;
 }
 
+// out[i * n_out + j] = src[row(i) * ld + col(j)] with row(i) = rows ? rows[i] : i and col(j)
+// likewise: the row sample and column permutation of the PERM objective in one pass.  Each
+// thread writes 4 consecutive outputs of one row (coalesced stores; the reads follow the
+// permutation within a row that stays in L1/L2).  Rows stride over gridDim.y.
+__global__ void __launch_bounds__(256) gather_f32_kernel(const float* __restrict__ src, int64_t ld,
+                                                         const int64_t* __restrict__ rows, int64_t nrow_out,
+                                                         const int64_t* __restrict__ cols, int64_t n_out,
+                                                         float* __restrict__ out) {
+  const int64_t j0 = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
+  if (j0 >= n_out) return;
+  int64_t c[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) c[u] = (j0 + u < n_out) ? (cols ? cols[j0 + u] : j0 + u) : 0;
+  for (int64_t i = blockIdx.y; i < nrow_out; i += gridDim.y) {
+    const float* __restrict__ s = src + (rows ? rows[i] : i) * ld;
+    float* __restrict__ o = out + i * n_out;
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (j0 + u < n_out) o[j0 + u] = s[c[u]];
+  }
+}
+
+// acc[c] = sum over rows of (x[r * ld + c] - y[r * ld + c])^2 in float64 (y == NULL: x^2).  A
+// CTA owns 32 columns: warp w sums rows w, w + 8, ... (lane = column, so each row read is one
+// 128-byte segment) in two alternating accumulators, then the eight warp partials are added
+// in warp order, so the result does not depend on scheduling.
+__global__ void __launch_bounds__(256) col_sqdiff_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                                         int64_t nrow, int64_t n, int64_t ld,
+                                                         double* __restrict__ acc) {
+  __shared__ double part[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  double s0 = 0.0, s1 = 0.0;
+  if (c < n) {
+    int64_t r = warp;
+    for (; r + 8 < nrow; r += 16) {
+      double a = x[r * ld + c], b = x[(r + 8) * ld + c];
+      if (y) {
+        a -= (double)y[r * ld + c];
+        b -= (double)y[(r + 8) * ld + c];
+      }
+      s0 += a * a;
+      s1 += b * b;
+    }
+    if (r < nrow) {
+      double a = x[r * ld + c];
+      if (y) a -= (double)y[r * ld + c];
+      s0 += a * a;
+    }
+  }
+  part[warp][lane] = s0 + s1;
+  __syncthreads();
+  if (warp == 0 && c < n) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) t += part[w][lane];
+    acc[c] = t;
+  }
+}
+
+int launch_gather_f32(const float* src, int64_t ld, const int64_t* rows, int64_t nrow_out, const int64_t* cols,
+                      int64_t n_out, float* out, cudaStream_t stream) {
+  if (nrow_out <= 0 || n_out <= 0) return 0;
+  const int64_t bx = (n_out + 1023) / 1024;
+  if (bx > INT32_MAX) return 2;
+  const int64_t by = nrow_out < 8192 ? nrow_out : 8192;
+  gather_f32_kernel<<<dim3((unsigned)bx, (unsigned)by), 256, 0, stream>>>(src, ld, rows, nrow_out, cols, n_out, out);
+  note_launch();
+  return 0;
+}
+
+int launch_col_sqdiff(const float* x, const float* y, int64_t nrow, int64_t n, int64_t ld, double* acc,
+                      cudaStream_t stream) {
+  if (n <= 0) return 0;
+  const int64_t bx = (n + 31) / 32;
+  if (bx > INT32_MAX) return 2;
+  col_sqdiff_kernel<<<(unsigned)bx, 256, 0, stream>>>(x, y, nrow, n, ld, acc);
+  note_launch();
+  return 0;
+}
+
 }  // namespace cpk

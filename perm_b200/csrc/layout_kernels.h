@@ -22,4 +22,10 @@ int64_t transpose_tiles(int64_t rows, int64_t cols, int elem_bytes);
 int launch_transpose_batch(const TrBatch& b, int elem_bytes, int64_t total_tiles, cudaStream_t stream);
 // bytes from mapped (pinned) host memory to device memory, read by a kernel
 int launch_fetch_host(void* dst, const void* src_mapped, int64_t bytes, cudaStream_t stream);
+// out [nrow_out, n_out] = src[row(i) * ld + col(j)] (int64 index lists, NULL = identity)
+int launch_gather_f32(const float* src, int64_t ld, const int64_t* rows, int64_t nrow_out, const int64_t* cols,
+                      int64_t n_out, float* out, cudaStream_t stream);
+// acc[c] = sum_r (x[r * ld + c] - y[r * ld + c])^2, y NULL meaning 0 (float64, fixed order)
+int launch_col_sqdiff(const float* x, const float* y, int64_t nrow, int64_t n, int64_t ld, double* acc,
+                      cudaStream_t stream);
 }  // namespace cpk

@@ -1,4 +1,4 @@
-// H += X^T X for a batch of activations X [T, d] (coldpress/hessians.py:455-470 hook
+// H += X^T X for a batch of activations X [T, d] (coldpress/hessians.py:137-152 hook
 // arithmetic: `x.float(); acc += x.T @ x`).
 //
 // Tensor-core kernel for sm_100a: TMA loads of X tiles (128-byte swizzle) into a 4-stage

@@ -78,7 +78,7 @@ def cholesky_inv_upper(H, damp=0.01, _max_tries=6):
     n = H.shape[0]
     if n % 64:
         raise ValueError(f"cholesky_inv_upper: n={n} must be a multiple of 64 on the CUDA path")
-    H_dev = torch.from_numpy(np.ascontiguousarray(H, dtype=np.float64)).cuda()
+    H_dev = torch.from_numpy(kq.host_array(H, np.float64)).cuda()
     U, _ = factor_u_dev(H_dev, np.arange(n), damp, _max_tries, out_f64=True, diag_host=np.diag(H))
     return np.ascontiguousarray(U.cpu().numpy())
 
@@ -126,12 +126,12 @@ def ef_encode(x, ttype, qw, H, n_iter=2, damp=0.01, act_order=True):
     H = np.asarray(H)
     diag = np.diag(H)
     order = np.argsort(-diag) if act_order else np.arange(n)
-    H_dev = torch.from_numpy(np.ascontiguousarray(H, dtype=np.float64)).cuda()
+    H_dev = torch.from_numpy(kq.host_array(H, np.float64)).cuda()
     U_dev, _ = factor_u_dev(H_dev, order, damp, diag_host=diag)
     del H_dev
-    x_dev = torch.from_numpy(np.ascontiguousarray(x, dtype=F32)).cuda()
+    x_dev = torch.from_numpy(kq.host_array(x, F32)).cuda()
     qw_dev = None if qw is None else torch.from_numpy(
-        np.ascontiguousarray(np.broadcast_to(np.asarray(qw, F32), (n,)))).cuda()
+        kq.host_array(np.broadcast_to(np.asarray(qw, F32), (n,)), F32)).cuda()
     raw, _ = ef_encode_dev(x_dev, ttype, qw_dev, prepare_u_dev(U_dev), order, n_iter)
     recon = kq.dequantize_dev(ttype, raw, n)
     return raw.cpu().numpy(), recon.cpu().numpy()
@@ -140,14 +140,14 @@ def ef_encode(x, ttype, qw, H, n_iter=2, damp=0.01, act_order=True):
 # ---------------------------------------------------------------------------- driver
 
 def _hessian_to_device(torch, st, perm=None):
-    """Stored Hessian components -> float64 [d, d] on the device (hessians.py:542-560
+    """Stored Hessian components -> float64 [d, d] on the device (hessians.py:225-245
     arithmetic); a permutation is applied on the host first (ef.py:289-290)."""
     from . import gguf_io
     h = st["h"]
     if perm is None and h.dtype == np.float16:
         d = h.shape[0]
-        h16 = torch.from_numpy(np.ascontiguousarray(h).view(np.int16)).cuda()
-        d32 = torch.from_numpy(st["diag32"]).cuda() if st["diag32"] is not None else None
+        h16 = torch.from_numpy(kq.host_array(h, h.dtype).view(np.int16)).cuda()
+        d32 = torch.from_numpy(kq.host_array(st["diag32"], np.float32)).cuda() if st["diag32"] is not None else None
         H = torch.empty((d, d), dtype=torch.float64, device="cuda")
         nat.check(nat.lib().cp_hessian_decode(nat.ptr(h16), nat.ptr(d32), float(st["hscale"]), d, nat.ptr(H),
                                               nat.stream_ptr(torch)), "hessian_decode")
@@ -159,7 +159,7 @@ def _hessian_to_device(torch, st, perm=None):
         np.fill_diagonal(Hn, st["diag32"].astype(np.float64))
     if perm is not None:
         Hn = Hn[np.ix_(perm, perm)]
-    return torch.from_numpy(np.ascontiguousarray(Hn)).cuda()
+    return torch.from_numpy(kq.host_array(Hn, Hn.dtype)).cuda()
 
 
 def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, perms=None, spacemap=None, dims=None,
@@ -250,7 +250,7 @@ def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, per
                     hess_dev[hk] = _hessian_to_device(torch, st, p)
                     diags[hk] = torch.diagonal(hess_dev[hk]).cpu().numpy()
             jobs.append(Job(name, tt, "EF" if mode.startswith("EF") else mode, x,
-                            None if qw is None else torch.from_numpy(np.ascontiguousarray(qw, np.float32)).cuda(),
+                            None if qw is None else torch.from_numpy(kq.host_array(qw, np.float32)).cuda(),
                             hk, None if fit_w is None else torch.from_numpy(fit_w).cuda()))
         raws, st = enc.run(jobs, hess_dev, diags, stats=True)
         dt = time.time() - t0

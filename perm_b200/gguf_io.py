@@ -7,7 +7,7 @@ reference's Hessian storage format.
   * imatrix_means(path)            {tensor: in_sum2 / count} (coldpress/ggufio.py:105-123)
   * save_hessians / load_hessian   per-tensor npz with float16 H / hscale, exact float32
                                    diagonal, hscale and n; the old family-keyed layout is
-                                   read too (coldpress/hessians.py:499-567)
+                                   read too (coldpress/hessians.py:185-245)
 """
 import os
 

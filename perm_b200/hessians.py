@@ -1,4 +1,4 @@
-"""Hessian collection on the GPU (coldpress/hessians.py:402-496).
+"""Hessian collection on the GPU (coldpress/hessians.py:85-183).
 
 The reference hook computes `x.float(); acc += (x.T @ x).to(cpu)` for every hooked matmul.
 Here the accumulator stays on the device in float32 and each batch's X^T X is accumulated by
@@ -66,7 +66,7 @@ def xtx_status(device=None, stream=None):
 
 
 def _block_index(gguf_name):
-    """Block index of a GGUF tensor name, or -1 for embd/output/norm (hessians.py:53-60)."""
+    """Block index of a GGUF tensor name, or -1 for embd/output/norm (hessians.py:54-61)."""
     if gguf_name.startswith("blk."):
         try:
             return int(gguf_name.split(".")[1])
@@ -76,7 +76,7 @@ def _block_index(gguf_name):
 
 
 def build_name_map(model, arch, n_layers):
-    """{module_name: gguf_base_name} through gguf's TensorNameMap, as hessians.py:63-82."""
+    """{module_name: gguf_base_name} through gguf's TensorNameMap, as hessians.py:64-82."""
     import gguf
     import torch.nn as nn
     inv = {v: k for k, v in gguf.MODEL_ARCH_NAMES.items()}

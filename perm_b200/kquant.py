@@ -57,10 +57,17 @@ def dequantize_dev(ttype, raw, n, out=None, stream=None):
     return out
 
 
+def host_array(a, dtype):
+    """Contiguous numpy array of `dtype` that torch.from_numpy may wrap: read-only inputs
+    (np.broadcast_to views, read-only memory maps) are copied first."""
+    arr = np.ascontiguousarray(a, dtype=dtype)
+    return arr if arr.flags.writeable else arr.copy()
+
+
 def _to_dev(torch, a, dtype):
     if isinstance(a, torch.Tensor):
         return a.to(device="cuda", dtype=dtype).contiguous()
-    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.dtype(str(dtype).split(".")[-1]))).cuda()
+    return torch.from_numpy(host_array(a, np.dtype(str(dtype).split(".")[-1]))).cuda()
 
 
 def quantize(ttype, x, qw=None):

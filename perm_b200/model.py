@@ -4,7 +4,7 @@ A model is described by its GGUF tensor names and shapes ([out, in] row-major, t
 ef.py reads from a GGUF), the k-quant type of each tensor and the Hessian that feeds its error
 feedback.  q/k/v share one input (and so one Hessian), gate/up share another; the GGUF
 Hessian files the reference's collector writes for them hold identical matrices
-(coldpress/hessians.py:455-470), so the encoder factorises each distinct input once.
+(coldpress/hessians.py:137-152), so the encoder factorises each distinct input once.
 
 Type maps:
   * "q2_k_mix" (Qwen3-0.6B recipe, paper/METHOD.md:72-73): Q2_K for attn_q, attn_k,

@@ -16,63 +16,90 @@ from . import _native as nat
 from . import kquant as kq
 
 
-def _as_index(torch, p, dev):
-    return p.to(device=dev, dtype=torch.long) if isinstance(p, torch.Tensor) else \
-        torch.as_tensor(np.asarray(p, dtype=np.int64), device=dev)
+def _dev_f32(torch, a):
+    """float32 CUDA tensor (contiguous) of a numpy array or tensor."""
+    if isinstance(a, torch.Tensor):
+        return a.to(device="cuda", dtype=torch.float32).contiguous()
+    return torch.from_numpy(kq.host_array(a, np.float32)).cuda()
 
 
-def _as_f32(torch, a, dev):
-    return a.to(device=dev, dtype=torch.float32) if isinstance(a, torch.Tensor) else \
-        torch.as_tensor(np.asarray(a, dtype=np.float32), device=dev)
+def _dev_index(torch, p):
+    if p is None:
+        return None
+    if isinstance(p, torch.Tensor):
+        return p.to(device="cuda", dtype=torch.int64).contiguous()
+    return torch.from_numpy(kq.host_array(p, np.int64)).cuda()
+
+
+def _gather(torch, src, ld, rows, nrow_out, cols, n_out):
+    out = torch.empty((nrow_out, n_out), dtype=torch.float32, device="cuda")
+    nat.check(nat.lib().cp_gather_f32(nat.ptr(src), ld, nat.ptr(rows), nrow_out, nat.ptr(cols), n_out,
+                                      nat.ptr(out), nat.stream_ptr(torch)), "gather_f32")
+    return out
+
+
+def _host_f64(torch, a):
+    if isinstance(a, torch.Tensor):
+        return a.detach().to("cpu", torch.float64).numpy()
+    return np.asarray(a, dtype=np.float64)
 
 
 def tensor_err(x, ttype, qw, perm=None, wvec=None, rows_sample=None, seed=0):
     """Weighted quant error of x under permutation `perm` at container `ttype`
     (objective.py:17-39): float types give 0.0, rows_sample draws the same rows as the
-    reference (numpy default_rng(seed).choice, sorted)."""
+    reference (numpy default_rng(seed).choice, sorted).  On the device: one gather kernel
+    (row sample and column permutation), the quantize and dequantize kernels, and one
+    per-column float64 squared-error kernel; the host finishes with the reference's own
+    float64 dot product of the n column errors with the weights."""
     if ttype in ("F16", "F32", "BF16"):
         return 0.0
-    torch = nat.torch_cuda()
-    dev = "cuda"
-    nrow = int(x.shape[0])
-    if rows_sample and nrow > rows_sample:
-        rng = np.random.default_rng(seed)
-        idx = np.sort(rng.choice(nrow, rows_sample, replace=False))
-        if isinstance(x, torch.Tensor):
-            x = x.index_select(0, torch.as_tensor(idx, device=x.device))
-        else:
-            x = np.asarray(x)[idx]
-    xd = _as_f32(torch, x, dev)
-    qd = None if qw is None else _as_f32(torch, qw, dev)
-    if perm is not None:
-        pi = _as_index(torch, perm, dev)
-        xd = xd.index_select(1, pi)
-        qd = qd.index_select(0, pi) if qd is not None else None
-    xd = xd.contiguous()
     if ttype not in kq.QUANTIZE:
         raise ValueError(f"no encoder for {ttype}")
-    recon = kq.roundtrip(xd, ttype, qd)
-    colerr = ((recon.double() - xd.double()) ** 2).sum(0)
-    if wvec is not None:   # float64, as numpy promotes it (exact for float32 inputs)
-        w = wvec.to(device=dev, dtype=torch.float64) if isinstance(wvec, torch.Tensor) else \
-            torch.as_tensor(np.asarray(wvec, dtype=np.float64), device=dev)
-        if perm is not None:
-            w = w.index_select(0, _as_index(torch, perm, dev))
-        return float((colerr * w).sum())
+    torch = nat.torch_cuda()
+    xd = _dev_f32(torch, x)
+    if xd.dim() != 2:
+        raise ValueError("x must be 2-D [nrow, n_per_row]")
+    nrow, n = int(xd.shape[0]), int(xd.shape[1])
+    rows = None
+    if rows_sample and nrow > rows_sample:
+        rng = np.random.default_rng(seed)
+        rows = _dev_index(torch, np.sort(rng.choice(nrow, rows_sample, replace=False)))
+    pi = _dev_index(torch, perm)
+    if rows is not None or pi is not None:
+        xd = _gather(torch, xd, n, rows, int(rows.numel()) if rows is not None else nrow, pi, n)
+    qd = None
+    if qw is not None:
+        qd = _dev_f32(torch, qw)
+        if pi is not None:
+            qd = _gather(torch, qd, n, None, 1, pi, n).view(n)
+    raw = kq.quantize_dev(ttype, xd, qd)
+    recon = kq.dequantize_dev(ttype, raw, n)
+    colerr = torch.empty(n, dtype=torch.float64, device="cuda")
+    nat.check(nat.lib().cp_col_sqdiff(nat.ptr(recon), nat.ptr(xd), int(xd.shape[0]), n, n, nat.ptr(colerr),
+                                      nat.stream_ptr(torch)), "col_sqdiff")
+    colerr = colerr.cpu().numpy()
+    p_host = None if perm is None else _host_f64(torch, perm).astype(np.int64)
+    if wvec is not None:   # float64, as numpy promotes it
+        w = _host_f64(torch, wvec)
+        return float((colerr * (w[p_host] if p_host is not None else w)).sum())
     if qd is not None:
-        return float((colerr * qd.double()).sum())
+        return float((colerr * qd.cpu().numpy().astype(np.float64)).sum())
     return float(colerr.sum())
 
 
 def col_log_rms(x, row_step=32768):
-    """Per-column log-RMS profile (objective.py:42-49): float64 sums of squares in row chunks."""
+    """Per-column log-RMS profile (objective.py:42-49): float64 column sums of squares on the
+    device (one kernel per row chunk of x when x is a host array, so only a chunk at a time
+    travels), then the n logs on the host."""
     torch = nat.torch_cuda()
-    nrow = int(x.shape[0])
-    acc = torch.zeros(int(x.shape[1]), dtype=torch.float64, device="cuda")
-    for r0 in range(0, nrow, row_step):
-        xc = x[r0:r0 + row_step]
-        xc = xc.to(device="cuda", dtype=torch.float64) if isinstance(xc, torch.Tensor) else \
-            torch.as_tensor(np.asarray(xc, dtype=np.float64), device="cuda")
-        acc += (xc ** 2).sum(0)
-    out = torch.log(torch.sqrt(acc / nrow) + 1e-12)
-    return out.cpu().numpy() if not isinstance(x, torch.Tensor) else out
+    nrow, n = int(x.shape[0]), int(x.shape[1])
+    acc = np.zeros(n, np.float64)
+    part = torch.empty(n, dtype=torch.float64, device="cuda")
+    step = nrow if isinstance(x, torch.Tensor) else max(1, row_step)
+    for r0 in range(0, nrow, step):
+        xc = _dev_f32(torch, x[r0:r0 + step])
+        nat.check(nat.lib().cp_col_sqdiff(nat.ptr(xc), None, int(xc.shape[0]), n, n, nat.ptr(part),
+                                          nat.stream_ptr(torch)), "col_sqdiff")
+        acc += part.cpu().numpy()
+    out = np.log(np.sqrt(acc / nrow) + 1e-12)
+    return torch.from_numpy(out).cuda() if isinstance(x, torch.Tensor) else out

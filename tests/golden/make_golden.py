@@ -2,7 +2,7 @@
 
 Run in a container where the reference coldpress package is importable:
 
-    python tests/golden/make_golden.py [--ref /path/to/reference]
+    python tests/golden/make_golden.py --ref /path/to/reference/source/tree
 
 It imports the reference's own kquant.py and ef.py, feeds them seeded synthetic inputs and
 stores inputs and outputs (bytes, reconstructions, the float32 U factor) as .npz files next
@@ -52,7 +52,7 @@ def correlated_hessian(n, T, rng):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="source tree of the reference (the directory holding coldpress/)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from coldpress import kquant as kq, ef

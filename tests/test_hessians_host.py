@@ -1,4 +1,4 @@
-"""Host logic of collect_hessians (coldpress/hessians.py:402-496) on the CPU: name mapping,
+"""Host logic of collect_hessians (coldpress/hessians.py:85-183) on the CPU: name mapping,
 token counts, input sharing between sibling projections and its per-batch verification.
 The device product is replaced by torch's float32 matmul here, so the result must equal the
 reference hook's arithmetic bit for bit."""

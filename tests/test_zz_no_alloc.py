@@ -3,7 +3,8 @@
 that cannot hand it a scratch buffer).  It keeps its per-row errors in a fixed array inside the
 library.  Checked through the C ABI against cp_ef_sweep, which takes a caller workspace: two
 calls in a row with different shapes and types must both give identical codes and
-compensated weights, and an oversized shape must be refused.
+compensated weights, the codes must also equal the CPU oracle's sweep (coldpress/ef.py:197-216
+restated) on sampled rows, and an oversized shape must be refused.
 
 This file is named so that pytest collects it last."""
 import ctypes
@@ -30,7 +31,7 @@ def _inputs(torch, nat, tt, nrow, n, seed):
     raw = kq.quantize_dev(tt, x, qw)
     dl, ml, *_ = kq.grid_params_dev(tt, raw, nrow, n)
     od = torch.from_numpy(order.astype(np.int32)).cuda()
-    return x, od, ut2, dl, ml
+    return x, od, U, ut2, dl, ml, order
 
 
 def _sweep(torch, nat, tt, x, od, ut2, dl, ml, noalloc):
@@ -58,13 +59,21 @@ def test_noalloc_sweep_matches_workspace_sweep_twice():
         pytest.skip("needs a CUDA device")
     # two calls in a row, different types and shapes: the second must not see the first's
     # leftovers in the shared scratch
+    from oracle import oracle as orc
     for tt, nrow, n, seed in (("Q2_K", 3000, 1024, 1), ("Q3_K", 1000, 2048, 2)):
-        x, od, ut2, dl, ml = _inputs(torch, nat, tt, nrow, n, seed)
+        x, od, U, ut2, dl, ml, order = _inputs(torch, nat, tt, nrow, n, seed)
         ml = ml if nat.GRID[tt][3] else None
         want_codes, want_w = _sweep(torch, nat, tt, x, od, ut2, dl, ml, noalloc=False)
         got_codes, got_w = _sweep(torch, nat, tt, x, od, ut2, dl, ml, noalloc=True)
         assert np.array_equal(got_codes, want_codes), f"{tt}: {np.count_nonzero(got_codes != want_codes)} codes differ"
         assert np.array_equal(got_w.view(np.int32), want_w.view(np.int32)), f"{tt}: compensated weights differ"
+        # the same rows through the oracle's sweep, given the same U and committed grid
+        rows = np.unique(np.r_[np.arange(40), np.linspace(0, nrow - 1, 24).astype(np.int64)])
+        dl_h = dl.view(nrow, -1).cpu().numpy()[rows]
+        ml_h = ml.view(nrow, -1).cpu().numpy()[rows] if ml is not None else np.zeros_like(dl_h)
+        o_codes, _ = orc.ef_sweep(x.cpu().numpy()[rows], order, U.cpu().numpy(), dl_h, ml_h, tt)
+        assert np.array_equal(got_codes[rows].astype(np.int32), o_codes), \
+            f"{tt}: {np.count_nonzero(got_codes[rows] != o_codes)} codes differ from the oracle"
 
 
 def test_noalloc_sweep_refuses_shapes_beyond_its_scratch():
