@@ -49,6 +49,16 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # the second workload of the line: the Llama-3-8B-shaped Q4_K_M-style encode (BASELINE
+    # config[4]), streamed through the device in batches of layers
+    ap.add_argument("--no-config4", action="store_true")
+    ap.add_argument("--config4-model", default="llama3-8b")
+    ap.add_argument("--config4-mixture", default="q4_k_m_style")
+    ap.add_argument("--config4-tokens", type=int, default=131072)
+    ap.add_argument("--config4-steps", type=int, default=2)
+    ap.add_argument("--config4-warmup", type=int, default=3)
+    ap.add_argument("--config4-budget-gb", type=float, default=0.0,
+                    help="device bytes per batch (0: 30%% of the memory free once the inputs are resident)")
     return ap.parse_args()
 
 
@@ -103,6 +113,104 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax), "samples": len(sm),
                 "reasons": sorted(reasons)}
+
+
+def bench_config(args, world):
+    """The `config` of both arms' lines (the reference arm times a bounded sample of it)."""
+    from perm_b200 import model
+    specs = model.tensor_specs(model.MODELS[args.model], args.mixture)
+    params = sum(s.params for s in specs)
+    return {"workload": f"{args.model}-shaped whole-model EF encode, {args.mixture} "
+                        f"({len(specs)} tensors, {params / 1e6:.1f} M params)",
+            "mixture": args.mixture, "n_iter": 2, "damp": 0.01, "act_order": True,
+            "hessian_tokens": args.hessian_tokens,
+            "l2": "inputs (3 GB weights + float64 Hessians) are larger than L2; no flush",
+            "parallelism": f"tensor/row-range shards over {world} GPU(s), NCCL gather of packed bytes"}
+
+
+# ----------------------------------------------------------------------------- reference as-is
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+# One worker of the as-is reference timing: imports coldpress from the unmodified install in
+# baseline/_ref, builds its tensor's seeded inputs, waits for the common start time, then runs
+# the reference's ef.ef_encode plus the statistics' stock roundtrip (ef.py:298) and prints its
+# seconds.  argv: ref_dir, kind ("config0" | layer tensor index), seed, start_at (epoch s).
+_REF_WORKER = r"""
+import json, sys, time
+import numpy as np
+ref_dir, kind, seed, start_at = sys.argv[1], sys.argv[2], int(sys.argv[3]), float(sys.argv[4])
+sys.path.insert(0, ref_dir)
+from coldpress import ef, kquant as kq
+rng = np.random.default_rng(seed)
+if kind == "config0":
+    nrow, n, tt = 3072, 1024, "Q2_K"
+    W = (rng.standard_normal((nrow, n)) * 0.02).astype(np.float32)
+    W[:, rng.choice(n, n // 100, replace=False)] *= 8.0
+    T = 8192
+else:
+    shapes = [(2048, 1024, "Q2_K"), (1024, 1024, "Q2_K"), (1024, 1024, "Q3_K"), (1024, 2048, "Q3_K"),
+              (3072, 1024, "Q2_K"), (3072, 1024, "Q2_K"), (1024, 3072, "Q3_K")]
+    nrow, n, tt = shapes[int(kind)]
+    W = (rng.standard_normal((nrow, n)) * 0.02).astype(np.float32)
+    T = 8192
+X = rng.standard_normal((T, n)).astype(np.float32) * rng.lognormal(0, 1, n).astype(np.float32)
+H = (X.T.astype(np.float64) @ X.astype(np.float64)) / T
+qw = np.diag(H).astype(np.float32)
+while time.time() < start_at:
+    time.sleep(0.01)
+t0 = time.time()
+ef.ef_encode(W, tt, qw, H, n_iter=2, damp=0.01, act_order=True)
+kq.roundtrip(W, tt, qw)
+t1 = time.time()
+print(json.dumps({"params": int(W.size), "seconds": t1 - t0, "late": t0 - start_at}))
+"""
+
+
+def reference_available():
+    return os.path.isdir(os.path.join(REF_DIR, "coldpress"))
+
+
+def _ref_workers(kinds, seed, threads_each, setup_s):
+    """Run one as-is reference worker per entry of `kinds` at once; returns their records."""
+    env = dict(os.environ)
+    if threads_each is not None:
+        for v in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+            env[v] = str(threads_each)
+    start_at = time.time() + setup_s
+    procs = [subprocess.Popen([sys.executable, "-c", _REF_WORKER, REF_DIR, str(k), str(seed + i), repr(start_at)],
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env, text=True)
+             for i, k in enumerate(kinds)]
+    out = []
+    for p in procs:
+        o, e = p.communicate(timeout=900)
+        if p.returncode != 0:
+            raise RuntimeError(f"reference worker failed: {e.strip()[-300:]}")
+        out.append(json.loads(o.strip().splitlines()[-1]))
+    return out
+
+
+def run_reference_as_is(seed):
+    """BASELINE's two CPU numbers for the reference itself, unmodified (baseline/_ref):
+    (i) one process with default BLAS threads on one config[0] tensor (3072 x 1024 Q2_K EF);
+    (ii) one single-threaded process per tensor of layer 0 of the 0.6B model (7 tensors,
+    25.2 M params), all at once on the host cores (OPENBLAS_NUM_THREADS=1)."""
+    if not reference_available():
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    nt = cpu_threads()
+    one = _ref_workers(["config0"], seed, None, 3.0)[0]
+    par = _ref_workers([str(i) for i in range(7)], seed, 1, 10.0)
+    wall = max(r["seconds"] + r["late"] for r in par)
+    params = sum(r["params"] for r in par)
+    return {"reference_as_is": {"value": one["params"] / one["seconds"] / 1e6, "unit": UNIT, "cores": nt,
+                                "kind": "reference", "seconds": one["seconds"],
+                                "sample": "coldpress.ef.ef_encode + stock roundtrip, unmodified, one process "
+                                          "(default BLAS threads), one config[0] tensor 3072x1024 Q2_K"},
+            "reference_parallel": {"value": params / wall / 1e6, "unit": UNIT, "cores": min(nt, 7),
+                                   "kind": "reference", "seconds": wall,
+                                   "sample": "coldpress.ef.ef_encode + stock roundtrip, unmodified, one "
+                                             "single-threaded process per tensor of layer 0 (7 tensors, "
+                                             "25.2 M params), run at once"}}
 
 
 # ----------------------------------------------------------------------------- CPU (oracle) arm
@@ -178,10 +286,12 @@ def reference_arm(args, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "reference CPU encoder (oracle port), one Qwen3-0.6B-shaped layer per step",
-                       "mixture": args.mixture, "n_iter": 2, "act_order": True, "damp": 0.01},
+            "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": nt, "kind": "port",
-                             "sample": "layer 0 of the Qwen3-0.6B-shaped model per step (7 tensors, 25.2 M params)"},
+                             "sample": "bounded sample of the workload per step: layer 0 of the Qwen3-0.6B-shaped "
+                                       "model (7 tensors, 25.2 M params), EF n_iter 2 + stock roundtrip through "
+                                       "the CPU restatement of the reference (numpy LAPACK factor, C fits and "
+                                       "sweeps, all host threads)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -190,13 +300,19 @@ def reference_arm(args, rank, world):
 # ----------------------------------------------------------------------------- GPU arm
 
 class Workload:
-    """Inputs of this rank's units, resident on the device."""
+    """Inputs of this rank's units, resident on the device.  stored=True keeps the Hessians in
+    the reference's storage form (float16 H / hscale + float32 diagonal, perm_b200.stream) for
+    a model encoded in batches (decoded per batch inside the step) instead of as float64."""
 
-    def __init__(self, torch, args, rank, world):
+    def __init__(self, torch, args, rank, world, model_name=None, mixture=None, tokens=None, stored=False):
         from perm_b200 import model, shard
         self.torch = torch
-        cfg = model.MODELS[args.model]
-        self.specs = model.tensor_specs(cfg, args.mixture)
+        model_name = model_name or args.model
+        mixture = mixture or args.mixture
+        tokens = tokens or args.hessian_tokens
+        self.model_name, self.mixture, self.tokens, self.stored_mode = model_name, mixture, tokens, stored
+        cfg = model.MODELS[model_name]
+        self.specs = model.tensor_specs(cfg, mixture)
         self.spec_by_name = {s.name: s for s in self.specs}
         metas = [shard.UnitMeta(s.name, s.ttype, s.mode, s.nrow, s.n, s.hkey, s.mode != "wRTN(attn0-diag)")
                  for s in self.specs]
@@ -204,15 +320,22 @@ class Workload:
         self.units = self.plan.units[rank]
         self.total_params = sum(s.params for s in self.specs)
         dims = model.hessian_dims(self.specs)
+        self.dims = dims
         need = set()
         for u in self.units:
             sp = self.spec_by_name[u.name]
             need.add(sp.hkey)
-        self.hess, self.diags = {}, {}
+        self.hess, self.diags, self.stored = {}, {}, {}
         for k in sorted(need):
-            H = model.synth_hessian(torch, dims[k], k, args.seed, "cuda", tokens=args.hessian_tokens)
-            self.hess[k] = H
-            self.diags[k] = torch.diagonal(H).cpu().numpy()
+            H = model.synth_hessian(torch, dims[k], k, args.seed, "cuda", tokens=tokens)
+            if stored:
+                from perm_b200 import stream as stm
+                self.stored[k] = stm.store_hessian(torch, H)
+                self.diags[k] = self.stored[k].diag_host
+                del H
+            else:
+                self.hess[k] = H
+                self.diags[k] = torch.diagonal(H).cpu().numpy()
         self.ef_keys = sorted({self.spec_by_name[u.name].hkey for u in self.units
                                if self.spec_by_name[u.name].mode == "EF"})
         # the rank's weights are views into one flat float32 buffer (e2e moves them with one
@@ -262,7 +385,7 @@ class Workload:
         """Per-step algorithmic work of this rank per kernel class."""
         from perm_b200 import kquant as kq
         fit_bytes = fit_evals = sweep_updates = sweep_bytes = 0.0
-        factor_flops = sum((2.0 / 3.0) * float(self.hess[k].shape[0]) ** 3 for k in self.ef_keys)
+        factor_flops = sum((2.0 / 3.0) * float(self.dims[k]) ** 3 for k in self.ef_keys)
         from perm_b200.shard import FIT_PASSES
         for u in self.units:
             sp = self.spec_by_name[u.name]
@@ -276,6 +399,67 @@ class Workload:
                 sweep_bytes += n_iter * (rows * sp.n * (4 + 1 + 4)) + n_iter * sp.n * sp.n * 2.0
         return {"fit_bytes": fit_bytes, "fit_evals": fit_evals, "sweep_updates": sweep_updates,
                 "sweep_bytes": sweep_bytes, "factor_flops": factor_flops}
+
+
+def roofline_record(prof, alg, steps, clk):
+    """Roofline of the dominant kernel, the error-feedback sweep, from this rank's algorithmic
+    work and the live CUDA-event time of its launches (the sweep leads the serialised device
+    time of a step).  The sweep is bound by ordered FP32 arithmetic, so the headline fraction
+    is 2 unfused FP32 operations per ordered update against the FP32 lane rate (148 SMs x 128
+    lanes x the SM clock sampled during the timed region; nominal: MEASURED_PEAKS.json has no
+    FP32 figure).  Its HBM view (algorithmic bytes and the DRAM traffic per launch against the
+    measured copy bandwidth) and the k-quant fit's and the FP64 factor's own rooflines are
+    kept beside it."""
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    hbm_src = "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback 6650 GB/s"
+    per_step = {c: (prof[c][0] / steps, prof[c][1] / steps) for c in prof}
+    sm_mhz = clk.get("sm_mhz") or 1965.0
+    fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12   # T lane-ops/s: FADD/FMUL/FFMA one lane-op each
+    fp32_src = f"nominal: 148 SMs x 128 FP32 lanes x {sm_mhz:.0f} MHz (sampled SM clock)"
+    sw_ms, sw_l = per_step["sweep"]
+    sw_l = max(1.0, sw_l)
+    out = {"kernel": "ef_sweep", "bound": "fp32_alu", "unit": "T fp32 lane-ops/s", "peak": fp32_peak,
+           "peak_source": fp32_src, "work": "2 unfused FP32 ops per ordered update",
+           "ms_per_step": sw_ms, "launches_per_step": sw_l,
+           "classes_ms_per_step": {c: round(per_step[c][0], 4) for c in per_step}}
+    if sw_ms > 0:
+        out["achieved"] = 2.0 * alg["sweep_updates"] / (sw_ms / 1e3) / 1e12
+        out["frac"] = out["achieved"] / fp32_peak
+        # DRAM bytes of one sweep launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) of
+        # the second step's first sweep launch of the default 0.6B workload on one B200
+        # measured 36.77 GB (31.37 read + 5.40 written) for 425.1 G ordered updates, 0.08649
+        # bytes per update; per launch here = that rate x this rank's updates per round (the
+        # error re-reads, the larger part, grow like the updates: n^2/32 bytes per row and
+        # round against n^2/2 updates)
+        traffic = 0.08649 * alg["sweep_updates"] / sw_l
+        alg_bytes = alg["sweep_bytes"] / sw_l
+        gbs = alg["sweep_bytes"] / (sw_ms / 1e3) / 1e9
+        out["traffic"] = traffic
+        out["traffic_unit"] = "DRAM bytes per launch (ncu rate, scaled by this rank's updates)"
+        out["hbm"] = {"achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "peak_source": hbm_src,
+                      "algorithmic_bytes_per_launch": alg_bytes, "traffic": traffic,
+                      "traffic_over_algorithmic": traffic / alg_bytes if alg_bytes else None}
+    fit_ms = per_step["fit"][0]
+    if fit_ms > 0:
+        ach = 20.0 * alg["fit_evals"] / (fit_ms / 1e3) / 1e12
+        out["fit"] = {"kernel": "kquant fit+pack", "bound": "fp32_alu", "achieved": ach, "peak": fp32_peak,
+                      "unit": "T fp32 lane-ops/s", "frac": ach / fp32_peak,
+                      "work": "~20 ops per candidate-element evaluation",
+                      "hbm_gbs": alg["fit_bytes"] / (fit_ms / 1e3) / 1e9, "ms_per_step": fit_ms}
+    fac_ms = per_step["factor"][0]
+    if fac_ms > 0 and alg["factor_flops"] > 0:
+        ach = alg["factor_flops"] / (fac_ms / 1e3) / 1e12
+        out["factor"] = {"kernel": "fp64 factor (mma.sync f64)", "bound": "fp64_tensor", "achieved": ach,
+                         "peak": 37.0, "unit": "FP64 TFLOP/s", "frac": ach / 37.0,
+                         "peak_source": "measured back-to-back mma.sync f64 loop on this part (probe)",
+                         "work": "(2/3) n^3 per factorisation; event spans overlap the fits, so a lower bound",
+                         "ms_per_step": fac_ms}
+    return out
 
 
 def gpu_arm(args, rank, world, local_rank):
@@ -348,53 +532,8 @@ def gpu_arm(args, rank, world, local_rank):
         ms = float(t.item())
     value = wl.total_params / (ms / 1e3) / 1e6
 
-    # dominant kernel class and its roofline (this rank's algorithmic work / its event time)
-    from perm_b200 import _native as _n  # noqa: F401
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except (OSError, ValueError):
-        pass
-    hbm = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    alg = wl.algorithmic()
-    per_step = {c: (prof[c][0] / args.steps, prof[c][1] / args.steps) for c in prof}
-    # The sweep is the dominant kernel by serialised device time (ncu launch list of this
-    # command).  Class event times cannot pick it: the factor chains run on side streams next
-    # to the fits, so their event spans include the overlap.
-    dom = "sweep" if per_step["sweep"][1] > 0 else max(("fit", "factor"), key=lambda c: per_step[c][0])
-    sm_mhz = clk.get("sm_mhz") or 1965.0
-    alu_peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # T fp32 lane-ops/s (FADD/FMUL/FFMA each one lane-op)
-    kms = per_step[dom][0]
-    nl = max(1.0, per_step[dom][1])
-    if dom == "sweep":
-        gbs = alg["sweep_bytes"] / (kms / 1e3) / 1e9
-        alu = {"achieved": 2.0 * alg["sweep_updates"] / (kms / 1e3) / 1e12, "peak": alu_peak,
-               "unit": "T fp32 lane-ops/s", "work": "2 unfused ops per ordered update"}
-    elif dom == "fit":
-        gbs = alg["fit_bytes"] / (kms / 1e3) / 1e9
-        alu = {"achieved": 20.0 * alg["fit_evals"] / (kms / 1e3) / 1e12, "peak": alu_peak,
-               "unit": "T fp32 lane-ops/s", "work": "~20 ops per candidate-element evaluation"}
-    else:
-        gbs = None
-        alu = {"achieved": alg["factor_flops"] / (kms / 1e3) / 1e12, "peak": 37.0,
-               "unit": "FP64 TFLOP/s (nominal peak)", "work": "(2/3) n^3 per factorisation"}
-    if alu.get("peak"):
-        alu["frac"] = alu["achieved"] / alu["peak"]
-    traffic = None
-    if dom == "sweep":
-        # DRAM bytes of one sweep launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) of
-        # the second step's first sweep launch of this default workload on one B200 measured
-        # 36.77 GB (31.37 read + 5.40 written) for 425.1 G ordered updates, 0.08649 bytes per
-        # update; per launch of this rank = that rate x this rank's updates per round
-        traffic = 0.08649 * alg["sweep_updates"] / max(1.0, nl)
-    roofline = {"kernel": {"fit": "kquant fit+pack", "sweep": "ef_sweep", "factor": "fp64 factor"}[dom],
-                "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                "frac": (gbs / hbm) if gbs is not None else None, "traffic": traffic,
-                "traffic_unit": "bytes per launch (ncu, scaled by this rank's updates)",
-                "peak_source": f"{peak_src} hbm_gbs", "launches_per_step": nl,
-                "ms_per_step": kms, "alu": alu,
-                "classes_ms_per_step": {c: round(per_step[c][0], 4) for c in per_step}}
+    roofline = roofline_record(prof, wl.algorithmic(), args.steps, clk)
+    total_params, n_tensors = wl.total_params, len(wl.specs)
 
     e2e = None
     if not args.no_e2e:
@@ -403,23 +542,133 @@ def gpu_arm(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(args.seed)
+        try:
+            cpu.update(run_reference_as_is(args.seed))
+        except (RuntimeError, subprocess.TimeoutExpired, ValueError) as e:
+            cpu["reference_as_is"] = {"unavailable": str(e)[:200]}
+
+    big = None
+    if not args.no_config4:
+        total_params = wl.total_params
+        del wl, jobs, outputs, flat, enc
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        big = measure_streamed(torch, dist, args, rank, world, local_rank)
+        wl = None
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "whole_model_seconds": ms / 1e3,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (random-init N(0,0.02) weights, synthetic X^T X Hessians)",
-                "config": {"workload": f"{args.model}-shaped whole-model EF encode, {args.mixture} "
-                                       f"({len(wl.specs)} tensors, {wl.total_params / 1e6:.1f} M params)",
-                           "mixture": args.mixture, "n_iter": 2, "damp": 0.01, "act_order": True,
-                           "hessian_tokens": args.hessian_tokens,
-                           "l2": "inputs (3 GB weights + float64 Hessians) are larger than L2; no flush",
-                           "parallelism": f"tensor/row-range shards over {world} GPU(s), NCCL gather of packed bytes"},
+                "config": bench_config(args, world),
                 "gpu_launches": int(launches), "roofline": roofline, "clocks": clk, "e2e": e2e,
                 "cpu_baseline": cpu, "stats_median_rel_err_vs_stock": float(np.median(
-                    [v["rel_err_vs_stock"] for v in st.values()])) if st else None}
+                    [v["rel_err_vs_stock"] for v in st.values()])) if st else None,
+                "config4": big}
         print(json.dumps(line), flush=True)
     return 0
+
+
+def measure_streamed(torch, dist, args, rank, world, local_rank):
+    """the Llama-3-8B-shaped model (32 layers, hidden 4096, 32 q / 8 kv
+    heads x 128, ffn 14336, vocab 128256; 8.03 B parameters, 129 Hessians up to d = 14336 from
+    131072 synthetic tokens) EF-encoded into the Q4_K_M-style mixture.  The weights (float32)
+    and the Hessians in storage form (float16 / hscale + float32 diagonal) are resident; one
+    step decodes every Hessian, factorises it, and encodes every tensor, in memory-bounded
+    batches of whole Hessian groups (Encoder.run_stream), then (N > 1) gathers the packed
+    bytes to rank 0.  Returns the `config4` record of the bench line (rank 0), or None."""
+    from perm_b200 import _native as nat
+    from perm_b200 import stream as stm
+    from perm_b200.encoder import Encoder
+    from perm_b200.shard import gather_to_rank0
+    t_setup = time.perf_counter()
+    wl = Workload(torch, args, rank, world, model_name=args.config4_model, mixture=args.config4_mixture,
+                  tokens=args.config4_tokens, stored=True)
+    jobs = wl.jobs()
+    sizes = wl.out_bytes()
+    my_bytes = int(sum(sizes))
+    flat = torch.empty(max(1, my_bytes), dtype=torch.uint8, device="cuda")
+    outputs, off = {}, 0
+    for u, sz, j in zip(wl.units, sizes, jobs):
+        rows = u.r1 - u.r0
+        outputs[j.name] = flat[off:off + sz].view(rows, sz // rows)
+        off += sz
+    if world > 1:
+        t = torch.tensor([my_bytes], dtype=torch.int64, device="cuda")
+        g = [torch.zeros(1, dtype=torch.int64, device="cuda") for _ in range(world)]
+        dist.all_gather(g, t)
+        all_sizes = [int(v.item()) for v in g]
+    else:
+        all_sizes = [my_bytes]
+    torch.cuda.synchronize()
+    free, _total = torch.cuda.mem_get_info()
+    budget = args.config4_budget_gb * 1e9 if args.config4_budget_gb > 0 else 0.30 * free
+    job_batches = stm.plan(jobs, wl.dims, budget)
+    enc = Encoder(n_iter=2, damp=0.01, act_order=True)
+    dec = torch.cuda.Stream(priority=-1)
+    setup_s = time.perf_counter() - t_setup
+
+    def step():
+        _, st = enc.run_stream(stm.batches(torch, job_batches, wl.stored, outputs, dec), stats=True)
+        if world > 1:
+            gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+        return st
+
+    if world > 1:
+        dist.barrier()
+    for _ in range(max(1, args.config4_warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = nat.lib().cp_launch_count()
+    nat.profile_enable(True)
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start.record()
+    for _ in range(args.config4_steps):
+        st = step()
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    nat.profile_enable(False)
+    launches = (nat.lib().cp_launch_count() - launches0) // max(1, args.config4_steps)
+    prof = nat.profile_collect()
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end) / args.config4_steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = wl.total_params / (ms / 1e3) / 1e6
+    roof = roofline_record(prof, wl.algorithmic(), args.config4_steps, clk)
+    peak_gb = torch.cuda.max_memory_allocated() / 1e9
+    rec = None
+    if rank == 0:
+        rec = {"workload": f"{args.config4_model}-shaped whole-model EF encode, {args.config4_mixture} "
+                           f"({len(wl.specs)} tensors, {wl.total_params / 1e6:.1f} M params)",
+               "metric": METRIC.replace("(Q2_K)", "(Q4_K_M-style)"), "value": value, "unit": UNIT,
+               "ms_per_step": ms, "whole_model_seconds": ms / 1e3, "steps": args.config4_steps,
+               "warmup": max(1, args.config4_warmup), "n_gpus": world, "hessian_tokens": args.config4_tokens,
+               "batches_per_step": len(job_batches), "batch_budget_gb": round(budget / 1e9, 2),
+               "resident": "float32 weights + storage-form Hessians (float16/hscale + float32 diagonal); "
+                           "each batch's Hessians decoded to float64 inside the step",
+               "l2": "inputs (32 GB weights at N=1) are larger than L2; no flush",
+               "gpu_launches": int(launches), "roofline": roof, "clocks": clk,
+               "peak_device_gb_rank0": round(peak_gb, 1), "setup_seconds": round(setup_s, 1),
+               "stats_median_rel_err_vs_stock": float(np.median([v["rel_err_vs_stock"] for v in st.values()]))
+               if st else None}
+    del enc, outputs, flat, jobs, wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return rec
 
 
 def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_sizes, rank, world):

@@ -49,6 +49,36 @@ class Factor:
     ut2: object = None        # sweep layout of U (cp_ef_prepare_u)
 
 
+@dataclass
+class Deferred:
+    """A run(defer=True) whose device work may still be running (Encoder.finish completes it)."""
+    jobs: list
+    raws: dict
+    factors: dict
+    pending: tuple
+    stats: bool
+    after_pack: object = None
+    errs_dev: object = None
+    errs_h: object = None
+    status_h: object = None
+    event: object = None
+
+
+@dataclass
+class StreamBatch:
+    """One batch of Encoder.run_stream: its jobs, their Hessians ({key: float64 [d, d] on the
+    device}) and host diagonals, optional output buffers, and the events after which the
+    weights (inputs_event, as in run()) and the Hessians of each size (ready_events, as in
+    factor()) are on the device.  `tag` is free for the caller."""
+    jobs: list
+    hessians: dict
+    diags: dict = None
+    outputs: dict = None
+    inputs_event: object = None
+    ready_events: dict = None
+    tag: object = None
+
+
 class Encoder:
     """Whole-model encoder.  overlap_sweeps: in run(), start each Hessian size's first-round
     sweeps as soon as that size's factors are done instead of after all of them (measured
@@ -68,10 +98,43 @@ class Encoder:
         self.stream = stream
         self.log = log
         self._ws = None
-        self._fws = None
-        self._fstreams = None
+        self._fws = {}            # n -> factor workspaces, reused in stream order
+        self._fstreams = {}       # n -> factorisation stream
+        self._fstage = {}         # n -> ring of [pinned act-order staging, event of its last read]
+        self._fstage_next = {}
 
     # ---------------------------------------------------------------- factorisation
+    def _fstream(self, n):
+        """The factorisation stream of Hessian size n: every chain of that size runs on it, so
+        a size's workspaces are reused in stream order from one call to the next."""
+        if n not in self._fstreams:
+            self._fstreams[n] = self.torch.cuda.Stream(priority=self.factor_priority)
+        return self._fstreams[n]
+
+    def _factor_ws(self, n, count):
+        """Workspaces of the first `count` Hessians of size n (kept across calls)."""
+        lst = self._fws.setdefault(n, [])
+        while len(lst) < count:
+            lst.append(self.torch.empty(nat.lib().cp_factor_workspace_bytes(n), dtype=self.torch.uint8,
+                                        device="cuda"))
+        return lst[:count]
+
+    def _order_staging(self, n, count):
+        """A pinned [count, n] int32 staging buffer for act orders, from a small ring per size;
+        waits (host) until the kernel that read the buffer's previous contents has run."""
+        ring = self._fstage.setdefault(n, [])
+        i = self._fstage_next.get(n, 0)
+        self._fstage_next[n] = (i + 1) % 3
+        while len(ring) <= i:
+            ring.append([None, None])
+        buf, ev = ring[i]
+        if ev is not None:
+            ev.synchronize()
+        if buf is None or buf.shape[0] < count:
+            buf = self.torch.empty((count, n), dtype=self.torch.int32).pin_memory()
+            ring[i][0] = buf
+        return ring[i], buf[:count]
+
     def factor(self, hessians, diags=None, _max_tries=6, check=True, ready_events=None, start_event=None):
         """hessians: {key: torch float64 [d, d] on the device}; diags: {key: host diag} if known.
         Returns {key: Factor}.  All first attempts go out as one batched call (same-size
@@ -85,20 +148,15 @@ class Encoder:
         L = nat.lib()
         keys = sorted(hessians, key=lambda k: -int(hessians[k].shape[0]))
         if not keys:
+            self._pending = (keys, None, hessians, diags, _max_tries)
+            self._factor_done = {}
             return {}
         sizes = sorted({int(hessians[k].shape[0]) for k in keys}, reverse=True)
         groups = {n: [k for k in keys if int(hessians[k].shape[0]) == n] for n in sizes}
-        sig = tuple((k, int(hessians[k].shape[0])) for k in keys)
-        if getattr(self, "_fsig", None) != sig:
-            # per-key factor workspaces and one pinned staging row of act orders per size group
-            self._fws = {k: torch.empty(L.cp_factor_workspace_bytes(int(hessians[k].shape[0])), dtype=torch.uint8,
-                                        device="cuda") for k in keys}
-            self._forder_host = {n: torch.empty((len(groups[n]), n), dtype=torch.int32).pin_memory() for n in sizes}
-            self._fsig = sig
-        if getattr(self, "_fstreams", None) is None or len(self._fstreams) < len(sizes):
-            self._fstreams = [torch.cuda.Stream(priority=self.factor_priority) for _ in range(max(4, len(sizes)))]
         main = self.stream if self.stream is not None else torch.cuda.current_stream()
-        status = torch.zeros(len(keys), dtype=torch.int32, device="cuda")
+        # each chain's first launch zeroes its status words on its own stream (a zeroing on
+        # the main stream could land after a chain that already ran ahead of it)
+        status = torch.empty(len(keys), dtype=torch.int32, device="cuda")
         slot = {k: i for i, k in enumerate(keys)}
         if start_event is not None:
             ready = start_event
@@ -110,12 +168,13 @@ class Encoder:
         # Each size group is one chain of batched steps on its own stream; the largest (the
         # critical path) is prepared and launched first, so its chain starts while the host
         # still prepares the smaller ones.
-        for gi, n in enumerate(sizes):
+        for n in sizes:
             grp = groups[n]
-            st = self._fstreams[gi]
+            st = self._fstream(n)
             st.wait_event(ready_events[n] if ready_events is not None and n in ready_events else ready)
             sp = nat.stream_ptr(torch, st)
-            oh = self._forder_host[n]
+            wss = self._factor_ws(n, len(grp))
+            entry, oh = self._order_staging(n, len(grp))
             ohn = oh.numpy()
             shifts = []
             for r, k in enumerate(grp):
@@ -131,13 +190,16 @@ class Encoder:
             # the act orders leave the pinned staging row through a kernel read, not a copy
             # engine, so they never wait behind bulk uploads queued on other streams
             nat.check(L.cp_fetch_host(nat.ptr(od), oh.data_ptr(), od.numel() * 4, sp), "fetch_host")
+            fetched = torch.cuda.Event()
+            fetched.record(st)
+            entry[1] = fetched
             for t_ in (od, ut2g):   # also read on the main stream (sweeps)
                 t_.record_stream(main)
             jobs = []
             for r, k in enumerate(grp):
                 U = ut2g[r, :n * n].view(n, n)
                 jobs.append(nat.FactorJob(hessians[k].data_ptr(), n, od[r].data_ptr(), shifts[r], U.data_ptr(),
-                                          self._fws[k].data_ptr(), status[slot[k]:slot[k] + 1].data_ptr()))
+                                          wss[r].data_ptr(), status[slot[k]:slot[k] + 1].data_ptr()))
                 out[k] = Factor(U, ohn[r].astype(np.int64), od[r], self.damp, ut2g[r])
             arr = nat.job_array(nat.FactorJob, jobs)
             nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
@@ -153,12 +215,16 @@ class Encoder:
             self.escalate(out)
         return out
 
-    def escalate(self, factors):
+    def escalate(self, factors, pending=None, st_host=None):
         """Read the status words of the last factor() call (one synchronisation) and redo, with
         the reference's damp escalation, every factorisation that hit a non-positive pivot.
+        pending / st_host: the record and host status words of an earlier deferred call.
         Returns the keys whose factors changed."""
-        keys, status, hessians, diags, max_tries = self._pending
-        st_host = status.cpu().numpy()
+        keys, status, hessians, diags, max_tries = pending if pending is not None else self._pending
+        if not keys:
+            return []
+        if st_host is None:
+            st_host = status.cpu().numpy()
         redone = []
         for i, k in enumerate(keys):
             if st_host[i] == 0:
@@ -171,7 +237,7 @@ class Encoder:
         return redone
 
     def run(self, jobs, hessians, diags=None, stats=True, outputs=None, inputs_event=None, ready_events=None,
-            after_pack=None):
+            after_pack=None, defer=False):
         """factor() + encode() with the factorisations overlapped with the round-1 fits: the
         factor chains start on side streams, the fits (which need no U) go first on this
         stream, and the status words are read once at the end; tensors whose Hessian needed
@@ -182,7 +248,11 @@ class Encoder:
         ready_events: as in factor().  after_pack(event, names): called as soon as the packed
         bytes of the named jobs are queued (event: recorded after them on this stream),
         before the statistics and the status read, so a caller can start copying them out;
-        called again for the jobs re-encoded after a damp escalation."""
+        called again for the jobs re-encoded after a damp escalation.
+        defer: return (raws, Deferred) without waiting for the device; the statistics and the
+        factor status words travel to pinned host memory behind the encode, and finish()
+        completes the call (escalation, statistics) later, so the host can queue the next
+        batch of tensors meanwhile (run_stream)."""
         main = self.stream if self.stream is not None else self.torch.cuda.current_stream()
         start = self.torch.cuda.Event()
         start.record(main)   # the Hessians are ready at this point of the stream
@@ -200,8 +270,26 @@ class Encoder:
         # the fits go out first, then the host launches the factor chains (side streams,
         # higher priority) while the GPU already works on the fits
         raws, st = self.encode(jobs, None, stats=stats, outputs=outputs, factor_fn=launch_factor,
-                               staged_inputs=staged, after_pack=after_pack)
+                               staged_inputs=staged, after_pack=after_pack, defer=defer)
         factors = made["f"] if "f" in made else launch_factor()[0]
+        if defer:
+            torch = self.torch
+            pending = self._pending
+            status = pending[1]
+            d = Deferred(jobs, raws, factors, pending, stats, after_pack)
+            with torch.cuda.stream(main):   # main waited for every chain before its first sweep
+                if st is not None:
+                    d.errs_h = torch.empty(st.shape, dtype=st.dtype).pin_memory()
+                    d.errs_h.copy_(st, non_blocking=True)
+                    d.errs_dev = st
+                if status is not None:
+                    for n in self._factor_done:   # (also when no EF job waited for a chain)
+                        main.wait_event(self._factor_done[n])
+                    d.status_h = torch.empty(status.shape, dtype=status.dtype).pin_memory()
+                    d.status_h.copy_(status, non_blocking=True)
+            d.event = torch.cuda.Event()
+            d.event.record(main)
+            return raws, d
         redone = set(self.escalate(factors))
         if redone:
             again = [j for j in jobs if j.mode == "EF" and j.hkey in redone]
@@ -210,6 +298,50 @@ class Encoder:
             st.update(s2)
         return raws, st
 
+    def finish(self, d):
+        """Complete a deferred run(): wait for its device work, redo (as run() does) the
+        factorisations that hit a non-positive pivot and the tensors that used them, and return
+        (raws, stats)."""
+        d.event.synchronize()
+        st = self._stats(d.jobs, d.errs_h.numpy()) if d.stats else {}
+        redone = set(self.escalate(d.factors, d.pending, d.status_h.numpy() if d.status_h is not None else None))
+        if redone:
+            again = [j for j in d.jobs if j.mode == "EF" and j.hkey in redone]
+            r2, s2 = self.encode(again, d.factors, stats=d.stats, outputs={j.name: d.raws[j.name] for j in again},
+                                 after_pack=d.after_pack)
+            st.update(s2)
+        return d.raws, st
+
+    def run_stream(self, batches, stats=True, on_batch=None):
+        """Encode a model too large for one device pass, batch by batch, with one batch in
+        flight ahead of the host: batch b is queued, then batch b - 1 is finished (the host
+        waits for it while the device works on b), then batch b + 1 is prepared and queued.
+        Batch b + 1's Hessian decodes and factor chains, queued on their own streams while the
+        device still runs batch b's sweeps, overlap them.  batches: an iterable of
+        StreamBatch, produced lazily (its inputs may be decoded or uploaded when it is
+        drawn).  on_batch(batch, raws, stats): called as each batch finishes.
+        Returns (raws, stats) over all batches."""
+        raws_all, st_all = {}, {}
+        inflight = []
+
+        def done(item):
+            b, d = item
+            r, st = self.finish(d)
+            raws_all.update(r)
+            st_all.update(st)
+            if on_batch is not None:
+                on_batch(b, r, st)
+
+        for b in batches:
+            _, d = self.run(b.jobs, b.hessians, b.diags, stats=stats, outputs=b.outputs,
+                            inputs_event=b.inputs_event, ready_events=b.ready_events, defer=True)
+            inflight.append((b, d))
+            while len(inflight) > 1:
+                done(inflight.pop(0))
+        while inflight:
+            done(inflight.pop(0))
+        return raws_all, st_all
+
     # ---------------------------------------------------------------- tensors
     def _arena(self, jobs):
         """Per-job scratch (codes, compensated weights, grid, sweep workspace, baseline bytes),
@@ -217,7 +349,8 @@ class Encoder:
         torch = self.torch
         L = nat.lib()
         cm = self.column_major
-        key = (cm,) + tuple((j.name, j.ttype, j.mode, int(j.x.shape[0]), int(j.x.shape[1])) for j in jobs)
+        # keyed by the jobs' shapes only, so successive batches of like layers share one arena
+        key = (cm,) + tuple((j.ttype, j.mode, int(j.x.shape[0]), int(j.x.shape[1])) for j in jobs)
         if getattr(self, "_arena_key", None) == key:
             return self._arena_views
         sizes = {"codes": 0, "wcur": 0, "grid": 0, "work": 0, "base": 0, "xt": 0, "ct": 0, "wt": 0}
@@ -271,7 +404,7 @@ class Encoder:
         return views
 
     def encode(self, jobs, factors, stats=True, outputs=None, factor_event=None, factor_fn=None,
-               staged_inputs=None, after_pack=None):
+               staged_inputs=None, after_pack=None, defer=False):
         """Encode every job with grouped launches; returns ({name: raw uint8 on device},
         {name: stats dict}).  factor_fn: called (instead of passing factors) once the first
         round's fits and grids are queued; returns (factors, factor_event).  staged_inputs:
@@ -431,16 +564,23 @@ class Encoder:
             packed = torch.cuda.Event()
             packed.record(main)
             after_pack(packed, [j.name for j in jobs])
-        st = {}
         if stats:
             block_call(L.cp_weighted_err_batch, werr_items(range(len(jobs)), 0), "weighted_err_batch")
-            e = errs.cpu().numpy()
-            for idx, j in enumerate(jobs):
-                e_ours = float(e[idx, 0])
-                e_base = e_ours if j.mode == "wRTN" else float(e[idx, 1])
-                st[j.name] = {"type": j.ttype, "mode": j.mode,
-                              "rel_err_vs_stock": e_ours / e_base - 1 if e_base else 0.0}
-        return {j.name: r for j, r in zip(jobs, raws)}, st
+        out = {j.name: r for j, r in zip(jobs, raws)}
+        if defer:   # the caller moves errs to the host behind the work (run(defer=True))
+            return out, (errs if stats else None)
+        return out, (self._stats(jobs, errs.cpu().numpy()) if stats else {})
+
+    @staticmethod
+    def _stats(jobs, e):
+        """encode_gguf's per-tensor statistics from the [jobs, 2] error sums (ours, stock)."""
+        st = {}
+        for idx, j in enumerate(jobs):
+            e_ours = float(e[idx, 0])
+            e_base = e_ours if j.mode == "wRTN" else float(e[idx, 1])
+            st[j.name] = {"type": j.ttype, "mode": j.mode,
+                          "rel_err_vs_stock": e_ours / e_base - 1 if e_base else 0.0}
+        return st
 
 
 def _al(n, a=64):
