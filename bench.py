@@ -401,6 +401,19 @@ class Workload:
                 "sweep_bytes": sweep_bytes, "factor_flops": factor_flops}
 
 
+def make_guard(dist, rank, world):
+    """RankGuard over the process group's store (N > 1): a rank whose step raises reports it,
+    the others stop before their next step's collectives.  A no-op context at N = 1."""
+    import contextlib
+    if world == 1:
+        class _Solo:
+            def step(self):
+                return contextlib.nullcontext()
+        return _Solo()
+    from perm_b200.shard import RankGuard
+    return RankGuard(dist.distributed_c10d._get_default_store(), rank, world)
+
+
 def roofline_record(prof, alg, steps, clk):
     """Roofline of the dominant kernel, the error-feedback sweep, from this rank's algorithmic
     work and the live CUDA-event time of its launches (the sweep leads the serialised device
@@ -467,7 +480,7 @@ def gpu_arm(args, rank, world, local_rank):
     import torch.distributed as dist
     from perm_b200 import _native as nat
     from perm_b200.encoder import Encoder
-    from perm_b200.shard import gather_to_rank0
+    from perm_b200.shard import gather_stats_to_rank0, gather_to_rank0
 
     torch.cuda.set_device(local_rank)
     nat.lib()
@@ -491,11 +504,14 @@ def gpu_arm(args, rank, world, local_rank):
         all_sizes = [my_bytes]
     enc = Encoder(n_iter=2, damp=0.01, act_order=True)
 
+    guard = make_guard(dist, rank, world)
+
     def step():
-        _, st = enc.run(jobs, {k: wl.hess[k] for k in wl.ef_keys}, {k: wl.diags[k] for k in wl.ef_keys},
-                        stats=True, outputs=outputs)
-        if world > 1:
-            gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+        with guard.step():
+            _, st = enc.run(jobs, {k: wl.hess[k] for k in wl.ef_keys}, {k: wl.diags[k] for k in wl.ef_keys},
+                            stats=True, outputs=outputs)
+            if world > 1:
+                gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
         return st
 
     if world > 1:
@@ -534,6 +550,7 @@ def gpu_arm(args, rank, world, local_rank):
 
     roofline = roofline_record(prof, wl.algorithmic(), args.steps, clk)
     total_params, n_tensors = wl.total_params, len(wl.specs)
+    merged = gather_stats_to_rank0(dist, st, rank, world)   # every rank's units, per tensor
 
     e2e = None
     if not args.no_e2e:
@@ -564,7 +581,8 @@ def gpu_arm(args, rank, world, local_rank):
                 "config": bench_config(args, world),
                 "gpu_launches": int(launches), "roofline": roofline, "clocks": clk, "e2e": e2e,
                 "cpu_baseline": cpu, "stats_median_rel_err_vs_stock": float(np.median(
-                    [v["rel_err_vs_stock"] for v in st.values()])) if st else None,
+                    [v["rel_err_vs_stock"] for v in merged.values()])) if merged else None,
+                "stats_tensors": len(merged) if merged else 0,
                 "config4": big}
         print(json.dumps(line), flush=True)
     return 0
@@ -581,8 +599,9 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
     from perm_b200 import _native as nat
     from perm_b200 import stream as stm
     from perm_b200.encoder import Encoder
-    from perm_b200.shard import gather_to_rank0
+    from perm_b200.shard import gather_stats_to_rank0, gather_to_rank0
     t_setup = time.perf_counter()
+    torch.cuda.reset_peak_memory_stats()
     wl = Workload(torch, args, rank, world, model_name=args.config4_model, mixture=args.config4_mixture,
                   tokens=args.config4_tokens, stored=True)
     jobs = wl.jobs()
@@ -609,10 +628,13 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
     dec = torch.cuda.Stream(priority=-1)
     setup_s = time.perf_counter() - t_setup
 
+    guard = make_guard(dist, rank, world)
+
     def step():
-        _, st = enc.run_stream(stm.batches(torch, job_batches, wl.stored, outputs, dec), stats=True)
-        if world > 1:
-            gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+        with guard.step():
+            _, st = enc.run_stream(stm.batches(torch, job_batches, wl.stored, outputs, dec), stats=True)
+            if world > 1:
+                gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
         return st
 
     if world > 1:
@@ -650,6 +672,7 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
     value = wl.total_params / (ms / 1e3) / 1e6
     roof = roofline_record(prof, wl.algorithmic(), args.config4_steps, clk)
     peak_gb = torch.cuda.max_memory_allocated() / 1e9
+    merged = gather_stats_to_rank0(dist, st, rank, world)
     rec = None
     if rank == 0:
         rec = {"workload": f"{args.config4_model}-shaped whole-model EF encode, {args.config4_mixture} "
@@ -663,8 +686,8 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
                "l2": "inputs (32 GB weights at N=1) are larger than L2; no flush",
                "gpu_launches": int(launches), "roofline": roof, "clocks": clk,
                "peak_device_gb_rank0": round(peak_gb, 1), "setup_seconds": round(setup_s, 1),
-               "stats_median_rel_err_vs_stock": float(np.median([v["rel_err_vs_stock"] for v in st.values()]))
-               if st else None}
+               "stats_median_rel_err_vs_stock": float(np.median([v["rel_err_vs_stock"] for v in merged.values()]))
+               if merged else None, "stats_tensors": len(merged) if merged else 0}
     del enc, outputs, flat, jobs, wl
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -843,7 +866,7 @@ def main():
         if args.impl == "reference":
             return reference_arm(args, rank, world)
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local_rank))
         try:
             return gpu_arm(args, rank, world, local_rank)

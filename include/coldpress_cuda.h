@@ -258,6 +258,14 @@ size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d);
 int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, void* workspace,
                       size_t ws_bytes, void* stream);
 
+/* Failure-path testing of the bounded waits (no counterpart in the reference): arms the
+ * calling thread's NEXT cp_xtx_accumulate so that its loader issues no loads for the 64-token
+ * step `skip_step` and every wait in that call gives up after wait_ns nanoseconds
+ * (1 us .. 2 s).  The waits on the unfilled stage then run out, the kernel stops, drains the
+ * loads it did issue, frees its tensor memory and sets the status word, so cp_xtx_status
+ * returns CP_ERR_TIMEOUT and the device stays usable.  Nothing else changes; one call only. */
+int cp_xtx_inject_stall(int skip_step, int64_t wait_ns);
+
 /* Synchronises `stream`, reads and clears the workspace status word: CP_OK, or
  * CP_ERR_TIMEOUT when a wait inside an earlier cp_xtx_accumulate ran out (its H is then
  * incomplete). */

@@ -103,6 +103,7 @@ def lib():
         "cp_xtx_workspace_bytes": ([I, I64, I64], SZ),
         "cp_xtx_accumulate": ([I, P, I64, I64, P, P, SZ, P], I),
         "cp_xtx_status": ([P, P], I),
+        "cp_xtx_inject_stall": ([I, I64], I),
         "cp_kquant_encode_batch": ([I, P, I, P], I),
         "cp_grid_params_batch": ([P, I, P], I),
         "cp_kquant_repack_batch": ([P, I, P], I),

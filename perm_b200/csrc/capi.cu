@@ -17,6 +17,9 @@ static_assert(cpk::kNoAllocScratchBytes == CP_NOALLOC_SCRATCH_BYTES,
 namespace {
 
 thread_local char g_err[512] = "";
+// cp_xtx_inject_stall: armed for the calling thread's next cp_xtx_accumulate only
+thread_local int g_xtx_stall_step = -1;
+thread_local int64_t g_xtx_stall_wait_ns = 0;
 
 int set_err(int code, const char* msg) {
   std::snprintf(g_err, sizeof(g_err), "%s", msg);
@@ -586,11 +589,23 @@ int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, 
   if (ws_bytes < p.ws_bytes) return set_err(CP_ERR_WORKSPACE, "workspace smaller than cp_xtx_workspace_bytes()");
   cudaStream_t s = (cudaStream_t)stream;
   ProfScope ps(kProfOther, s);
-  const int rc = cpk::launch_xtx(x, dtype == CP_XTX_F32, T, d, H, workspace, p, s);
+  const int skip = g_xtx_stall_step;
+  const unsigned long long wait_ns = (unsigned long long)g_xtx_stall_wait_ns;
+  g_xtx_stall_step = -1;   // one-shot
+  g_xtx_stall_wait_ns = 0;
+  const int rc = cpk::launch_xtx(x, dtype == CP_XTX_F32, T, d, H, workspace, p, s, skip, wait_ns);
   if (rc == 1) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: kernel attribute or memset failed");
   if (rc == 2) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: cuTensorMapEncodeTiled unavailable from the driver");
   if (rc == 3) return set_err(CP_ERR_CUDA, "cp_xtx_accumulate: cuTensorMapEncodeTiled rejected the activation layout");
   return check_launch("cp_xtx_accumulate");
+}
+
+int cp_xtx_inject_stall(int skip_step, int64_t wait_ns) {
+  if (skip_step < 0 || wait_ns < 1000 || wait_ns > 2000000000LL)
+    return set_err(CP_ERR_ARG, "cp_xtx_inject_stall: skip_step >= 0 and 1 us <= wait_ns <= 2 s");
+  g_xtx_stall_step = skip_step;
+  g_xtx_stall_wait_ns = wait_ns;
+  return CP_OK;
 }
 
 int cp_xtx_status(void* workspace, void* stream) {

@@ -43,6 +43,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <atomic>
 #include <mutex>
 #include "xtx_kernels.h"
 #include "kquant_kernels.h"
@@ -63,7 +64,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;        // warp 0 TMA, warp 1 MMA, 
 constexpr int kChunkSteps = 8;                       // 64-token steps per TMEM accumulation chain
 constexpr uint32_t kTmemCols = 2 * kBN;              // two accumulators (double buffer)
 constexpr int kPartialFloats = kBM * kBN;            // 128 KB per (tile, split) partial
-constexpr unsigned long long kWaitNs = 1000000000ull;
+constexpr unsigned long long kWaitNs = 1000000000ull;   // default bound of every mbarrier wait
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
 
 // UMMA instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12
@@ -78,6 +79,9 @@ struct XtxParams {
   int steps_per_split;
   float* partial;    // [splits][tiles][2][4][128][32] when splits > 1
   int* status;       // sticky error word
+  unsigned long long wait_ns;   // bound of every mbarrier wait
+  int skip_step;     // failure-path tests only: the producer issues no loads for this 64-token
+                     // step (its stage is never filled, so the waits on it run out); -1 = none
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -108,14 +112,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity.  False when it ran out or another role
-// of this CTA gave up (abort word nonzero).
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort) {
+// Bounded wait for the phase with the given parity.  False when it ran out (limit_ns of
+// global time) or another role of this CTA gave up (abort word nonzero).
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort,
+                                          unsigned long long limit_ns) {
   if (mbar_try(a, parity)) return true;
   const unsigned long long t0 = gtime();
   for (uint32_t n = 1; n < (1u << 30); n++) {
     if (mbar_try(a, parity)) return true;
-    if ((n & 255) == 0 && (*abort || gtime() - t0 > kWaitNs)) return false;
+    if ((n & 255) == 0 && (*abort || gtime() - t0 > limit_ns)) return false;
   }
   return false;
 }
@@ -298,11 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < kStages; s++) last_round[s] = -1;
       for (int g = g0, it = 0; g < g1; g++, it++) {
         const int st = it % kStages, round = it / kStages;
-        if (round > 0 && !mbar_wait(empty0 + 8 * st, (round - 1) & 1, abort)) {
+        if (round > 0 && !mbar_wait(empty0 + 8 * st, (round - 1) & 1, abort, prm.wait_ns)) {
           *abort = 1;
           atomicOr(prm.status, 1);
           break;
         }
+        if (g == prm.skip_step) continue;   // failure-path test: this stage stays empty
         const int phase = g / prm.ki, t0 = (g % prm.ki) * kBK;
         const CUtensorMap* ma = phase < 2 ? &map_hi : &map_lo;
         const CUtensorMap* mb = (phase & 1) ? &map_lo : &map_hi;
@@ -319,9 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every load this thread issued lands before the CTA exits
       for (int s = 0; s < kStages; s++)
-        if (last_round[s] >= 0 && !mbar_wait(full0 + 8 * s, last_round[s] & 1, abort)) {
+        if (last_round[s] >= 0 && !mbar_wait(full0 + 8 * s, last_round[s] & 1, abort, prm.wait_ns)) {
           int zero = 0;
-          mbar_wait(full0 + 8 * s, last_round[s] & 1, &zero);
+          mbar_wait(full0 + 8 * s, last_round[s] & 1, &zero, prm.wait_ns);
         }
     }
   } else if (warp == 1) {
@@ -331,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int c = 0; c < nchunks && ok; c++) {
         const int b = c & 1;
-        if (c >= 2 && !mbar_wait(acce0 + 8 * b, ((c >> 1) - 1) & 1, abort)) {
+        if (c >= 2 && !mbar_wait(acce0 + 8 * b, ((c >> 1) - 1) & 1, abort, prm.wait_ns)) {
           ok = false;
           break;
         }
@@ -340,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ge = min(g1, g0 + (c + 1) * kChunkSteps);
         for (int g = g0 + c * kChunkSteps, k = 0; g < ge; g++, it++, k++) {
           const int st = it % kStages, round = it / kStages;
-          if (!mbar_wait(full0 + 8 * st, round & 1, abort)) {
+          if (!mbar_wait(full0 + 8 * st, round & 1, abort, prm.wait_ns)) {
             ok = false;
             break;
           }
@@ -366,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // all MMAs issued above complete before TMEM is freed
       umma_commit(done_bar);
       int zero = 0;
-      mbar_wait(done_bar, 0, &zero);
+      mbar_wait(done_bar, 0, &zero, prm.wait_ns);
     }
   } else {
     // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (tile rows) and the 128
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int c = 0; c < nchunks; c++) {
       const int b = c & 1;
-      const bool got = mbar_wait(accf0 + 8 * b, (c >> 1) & 1, abort);
+      const bool got = mbar_wait(accf0 + 8 * b, (c >> 1) & 1, abort, prm.wait_ns);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
@@ -592,13 +598,17 @@ XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms) {
 }
 
 int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, void* ws, const XtxPlan& p,
-               cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(xtx_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-        cudaSuccess)
-      return 1;
-    attr_set = true;
+               cudaStream_t stream, int skip_step, unsigned long long wait_ns) {
+  {  // the kernel's dynamic shared memory exceeds the 48 KB default: opt in once per device
+    static std::atomic<unsigned long long> opted{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+    if (!(opted.load() & (1ULL << dev))) {
+      if (cudaFuncSetAttribute(xtx_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+          cudaSuccess)
+        return 1;
+      opted.fetch_or(1ULL << dev);
+    }
   }
   uint8_t* w = static_cast<uint8_t*>(ws);
   const void* hi = x;
@@ -626,6 +636,8 @@ int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, voi
   prm.steps_per_split = p.steps_per_split;
   prm.partial = reinterpret_cast<float*>(w + p.off_partial);
   prm.status = reinterpret_cast<int*>(w);
+  prm.wait_ns = wait_ns ? wait_ns : kWaitNs;
+  prm.skip_step = skip_step;
   xtx_tc_kernel<<<p.tiles * p.splits, kThreads, kSmemBytes, stream>>>(mh, ml, prm);
   note_launch();
   if (p.splits > 1) {

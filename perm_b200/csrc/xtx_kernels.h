@@ -18,7 +18,9 @@ struct XtxPlan {
 };
 
 XtxPlan xtx_plan(int64_t T, int64_t d, int f32_input, int num_sms);
+// skip_step >= 0 (failure-path tests only): no loads are issued for that 64-token step, so
+// the waits on it run out after wait_ns (0: the default bound of about one second).
 int launch_xtx(const void* x, int f32_input, int64_t T, int64_t d, float* H, void* ws, const XtxPlan& p,
-               cudaStream_t stream);
+               cudaStream_t stream, int skip_step = -1, unsigned long long wait_ns = 0);
 
 }  // namespace cpk

@@ -579,7 +579,8 @@ class Encoder:
             e_ours = float(e[idx, 0])
             e_base = e_ours if j.mode == "wRTN" else float(e[idx, 1])
             st[j.name] = {"type": j.ttype, "mode": j.mode,
-                          "rel_err_vs_stock": e_ours / e_base - 1 if e_base else 0.0}
+                          "rel_err_vs_stock": e_ours / e_base - 1 if e_base else 0.0,
+                          "err": e_ours, "err_stock": e_base}
         return st
 
 

@@ -14,6 +14,7 @@ Greedy LPT: units sorted by cost, each to the rank whose load (including any fac
 it would newly need) grows least.  Units of one Hessian group are kept whole unless they
 exceed a fair share, so U is usually computed once per node.
 """
+import contextlib
 from dataclasses import dataclass, field
 
 # candidate evaluations per element of one fit (kquant.py: 1 + nstep+1 candidates for qkx,
@@ -129,3 +130,90 @@ def gather_to_rank0(torch, dist, flat, sizes, rank, world):
         for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, flat, 0)]):
             req.wait()
     return None
+
+
+def unit_tensor(name):
+    """Tensor name of a unit id `name[r0:r1]` (the name itself when it carries no row range)."""
+    return name.split("[", 1)[0] if name.endswith("]") and "[" in name else name
+
+
+def merge_unit_stats(stats):
+    """Per-tensor statistics from per-unit ones ({unit id: stats dict with "err" and
+    "err_stock", the weighted squared-error sums of the encode and of the stock baseline}):
+    the sums of a tensor's row ranges add, so rel_err_vs_stock = sum(err) / sum(err_stock) - 1
+    is the same number a single-device encode of the whole tensor reports (up to float64
+    summation order)."""
+    out = {}
+    for name, st in stats.items():
+        t = unit_tensor(name)
+        o = out.setdefault(t, {"type": st.get("type"), "mode": st.get("mode"), "err": 0.0, "err_stock": 0.0})
+        o["err"] += float(st["err"])
+        o["err_stock"] += float(st["err_stock"])
+    for o in out.values():
+        o["rel_err_vs_stock"] = o["err"] / o["err_stock"] - 1 if o["err_stock"] else 0.0
+    return out
+
+
+def gather_stats_to_rank0(dist, stats, rank, world):
+    """Per-unit statistics of every rank, merged per tensor on rank 0 (None elsewhere).  The
+    error sums travel as Python objects through the process group (a few KB)."""
+    if world == 1:
+        return merge_unit_stats(stats)
+    got = [None] * world if rank == 0 else None
+    dist.gather_object(stats, got, dst=0)
+    if rank != 0:
+        return None
+    allst = {}
+    for d in got:
+        allst.update(d)
+    return merge_unit_stats(allst)
+
+
+class RankFailure(RuntimeError):
+    """Another rank reported a failure between steps."""
+
+
+class RankGuard:
+    """Host-side failure detection between the steps of a multi-rank encode.
+
+    A rank whose step raises writes its rank and error to the process group's store before
+    leaving; every rank checks that key before it starts a step (and so before the step's
+    collectives) and raises RankFailure naming the failed rank instead of entering a
+    collective that would wait for it.  A rank that dies without reaching the store, or fails
+    while the others are already inside a collective, is caught by the process group's
+    timeout, which callers keep short.  No device work is involved: a failed rank leaves only
+    between steps, with none of its kernels or collectives in flight."""
+
+    def __init__(self, store, rank, world, key="perm_b200/failed"):
+        self.store, self.rank, self.world, self.key = store, rank, world, key
+
+    def failed(self):
+        """(rank, message) of a reported failure, or None."""
+        if not self.store.check([self.key]):
+            return None
+        v = self.store.get(self.key).decode(errors="replace")
+        r, _, msg = v.partition(":")
+        return int(r), msg
+
+    def check(self):
+        f = self.failed()
+        if f is not None:
+            raise RankFailure(f"rank {f[0]} failed: {f[1]}")
+
+    def report(self, exc):
+        try:
+            self.store.set(self.key, f"{self.rank}:{type(exc).__name__}: {exc}"[:500])
+        except Exception:   # the store itself may be gone; the timeout still bounds the others
+            pass
+
+    @contextlib.contextmanager
+    def step(self):
+        """with guard.step(): ... -- checks for an earlier failure first, reports this rank's."""
+        self.check()
+        try:
+            yield
+        except RankFailure:
+            raise
+        except BaseException as e:
+            self.report(e)
+            raise

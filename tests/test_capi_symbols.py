@@ -41,3 +41,11 @@ def test_shape_errors_need_no_gpu():
     assert rc == nat.CP_ERR_SHAPE and "multiple" in nat.last_error()
     rc = L.cp_kquant_encode(99, None, 4, 256, None, None, None)
     assert rc == nat.CP_ERR_TYPE
+
+
+def test_xtx_inject_stall_checks_its_arguments():
+    from perm_b200 import _native as nat
+    L = nat.lib()
+    assert L.cp_xtx_inject_stall(-1, 2_000_000) == nat.CP_ERR_ARG
+    assert L.cp_xtx_inject_stall(0, 10) == nat.CP_ERR_ARG
+    assert L.cp_xtx_inject_stall(0, 5_000_000_000) == nat.CP_ERR_ARG

@@ -74,3 +74,114 @@ def test_gather_to_rank0_with_gloo_ranks():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert got == [[0, 1, 2, 3, 4], [], [20, 21, 22, 23, 24, 25, 26]]
+
+
+def test_merge_unit_stats_adds_row_range_sums():
+    from perm_b200.shard import merge_unit_stats, unit_tensor
+    assert unit_tensor("output.weight[0:100]") == "output.weight"
+    assert unit_tensor("blk.0.attn_q.weight") == "blk.0.attn_q.weight"
+    st = {"output.weight[0:10]": {"type": "Q6_K", "mode": "EF", "err": 1.0, "err_stock": 2.0},
+          "output.weight[10:30]": {"type": "Q6_K", "mode": "EF", "err": 3.0, "err_stock": 2.0},
+          "blk.0.ffn_up.weight[0:3072]": {"type": "Q2_K", "mode": "EF", "err": 9.0, "err_stock": 10.0}}
+    m = merge_unit_stats(st)
+    assert set(m) == {"output.weight", "blk.0.ffn_up.weight"}
+    assert m["output.weight"]["rel_err_vs_stock"] == 4.0 / 4.0 - 1
+    assert abs(m["blk.0.ffn_up.weight"]["rel_err_vs_stock"] + 0.1) < 1e-12
+
+
+def _init(rank, world, port, timeout_s):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    return dist
+
+
+def _stats_worker(rank, world, port, out):
+    dist = _init(rank, world, port, 60)
+    try:
+        from perm_b200.shard import gather_stats_to_rank0
+        mine = {f"output.weight[{10 * rank}:{10 * rank + 10}]": {"type": "Q6_K", "mode": "EF",
+                                                                 "err": float(rank + 1), "err_stock": 2.0}}
+        m = gather_stats_to_rank0(dist, mine, rank, world)
+        if rank == 0:
+            out.put(m)
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world, extra=()):
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + tuple(extra)) for r in range(world)]
+    for p in procs:
+        p.start()
+    return procs, q
+
+
+def test_stats_gather_merges_every_rank():
+    procs, q = _spawn(_stats_worker, 3)
+    m = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert abs(m["output.weight"]["rel_err_vs_stock"] - (6.0 / 6.0 - 1)) < 1e-12
+
+
+def _failing_worker(rank, world, port, out, fail_rank, fail_step):
+    """Steps of one all-reduce each under a RankGuard; `fail_rank` raises between steps."""
+    import time
+    import torch
+    dist = _init(rank, world, port, 5)
+    from perm_b200.shard import RankFailure, RankGuard
+    guard = RankGuard(dist.distributed_c10d._get_default_store(), rank, world)
+    t0 = time.time()
+    outcome = "completed"
+    try:
+        for step in range(6):
+            with guard.step():
+                if rank == fail_rank and step == fail_step:
+                    raise ValueError("injected host failure")
+                t = torch.ones(4)
+                dist.all_reduce(t)
+                time.sleep(0.05)
+    except RankFailure as e:
+        outcome = f"RankFailure: {e}"
+    except ValueError as e:
+        outcome = f"raised: {e}"
+    except Exception as e:  # the process group's timeout ended a collective
+        outcome = f"collective error: {type(e).__name__}"
+    out.put((rank, outcome, time.time() - t0))
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def test_a_failing_rank_ends_the_others_without_a_hang():
+    """One gloo rank raises between steps: it reports through the store, and every other rank
+    ends with an error (RankFailure before its next step, or the short process-group timeout
+    of a collective it had already entered) well within the bound, instead of hanging."""
+    world, fail_rank = 3, 1
+    procs, q = _spawn(_failing_worker, world, (fail_rank, 2))
+    res = {}
+    for _ in range(world):
+        r, outcome, dt = q.get(timeout=120)
+        res[r] = (outcome, dt)
+    for p in procs:
+        p.join(timeout=60)
+        if p.exitcode is None:
+            p.kill()
+    assert res[fail_rank][0].startswith("raised: injected")
+    for r in range(world):
+        if r == fail_rank:
+            continue
+        outcome, dt = res[r]
+        assert outcome.startswith("RankFailure: rank 1 failed") or outcome.startswith("collective error"), outcome
+        assert dt < 30.0

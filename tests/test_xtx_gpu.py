@@ -183,3 +183,28 @@ def test_collect_hessians_matches_reference_hook(dtype):
     solo, _ = hessians.collect_hessians(model, batches, ne0, "llama", 2, log=lambda *a: None, share_inputs=False)
     for k in got:
         assert np.array_equal(got[k]["H"], solo[k]["H"]), k
+
+
+@pytest.mark.parametrize("dtype_name,T,d,skip", [("bf16", 4096, 512, 5), ("f32", 2048, 256, 70)])
+def test_xtx_bounded_wait_runs_out_and_reports_timeout(dtype_name, T, d, skip):
+    """The failure path of the bounded waits, made on the host: cp_xtx_inject_stall arms the
+    next call so that its loader issues nothing for one 64-token step, and every wait gives up
+    after 2 ms.  The kernel must stop, report CP_ERR_TIMEOUT through cp_xtx_status and leave
+    the device usable: the next (unarmed) call on the same workspace is correct again."""
+    torch, nat, L = _lib()
+    dtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    x = _acts(torch, T, d, 11, dtype)
+    dt = nat.CP_XTX_BF16 if dtype_name == "bf16" else nat.CP_XTX_F32
+    ws = torch.zeros(max(L.cp_xtx_workspace_bytes(dt, T, d), 256), dtype=torch.uint8, device="cuda")
+    s = nat.stream_ptr(torch)
+    assert L.cp_xtx_inject_stall(skip, 2_000_000) == nat.CP_OK
+    H = torch.zeros(d, d, device="cuda")
+    assert L.cp_xtx_accumulate(dt, nat.ptr(x), T, d, nat.ptr(H), nat.ptr(ws), ws.numel(), s) == nat.CP_OK
+    rc = L.cp_xtx_status(nat.ptr(ws), s)
+    assert rc == nat.CP_ERR_TIMEOUT, nat.last_error()
+    assert "ran out" in nat.last_error()
+    # the status word was cleared, nothing is left armed, and the device still computes
+    H2 = _run(torch, nat, L, x, torch.zeros(d, d, device="cuda"))
+    ref = x.double().T @ x.double()
+    f32 = x.float().T @ x.float()
+    assert _err(H2, ref, ref) <= 4 * max(_err(f32, ref, ref), FLOOR)
