@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # the second workload of the line: the Llama-3-8B-shaped Q4_K_M-style encode (BASELINE
     # config[4]), streamed through the device in batches of layers
+    ap.add_argument("--no-gguf", action="store_true")
     ap.add_argument("--no-config4", action="store_true")
     ap.add_argument("--config4-model", default="llama3-8b")
     ap.add_argument("--config4-mixture", default="q4_k_m_style")
@@ -556,6 +557,10 @@ def gpu_arm(args, rank, world, local_rank):
     if not args.no_e2e:
         e2e = measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_sizes, rank, world)
 
+    gguf_rec = None
+    if world == 1 and not args.no_gguf:
+        gguf_rec = measure_gguf(torch, args, wl)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(args.seed)
@@ -583,9 +588,88 @@ def gpu_arm(args, rank, world, local_rank):
                 "cpu_baseline": cpu, "stats_median_rel_err_vs_stock": float(np.median(
                     [v["rel_err_vs_stock"] for v in merged.values()])) if merged else None,
                 "stats_tensors": len(merged) if merged else 0,
+                "whole_model_seconds_gguf": gguf_rec,
                 "config4": big}
         print(json.dumps(line), flush=True)
     return 0
+
+
+def measure_gguf(torch, args, wl):
+    """Whole-model seconds through the file formats (N = 1): the same 0.6B-shaped model written
+    to local disk as the reference's encode inputs -- a float16 GGUF of the weights, a target
+    GGUF of the Q2_K mixture, one compressed Hessian npz per tensor in the reference's storage
+    form (hessians.py:185-207) and an imatrix GGUF holding diag(H) -- then encoded by
+    perm_b200.ef.encode_gguf (the drop-in for ef.py:223-317), which reads, decodes, encodes
+    and re-emits the GGUF.  One warm-up run, then one timed run; the files sit in the page
+    cache (written just before).  Returns the record of the bench line."""
+    import concurrent.futures as cf
+    import shutil
+    import tempfile
+    import gguf
+    from gguf import GGUFWriter
+    from perm_b200 import ef, gguf_io, kquant as kq
+    t0 = time.perf_counter()
+    tmp = tempfile.mkdtemp(prefix="perm_b200_gguf_")
+    try:
+        f16p, tgtp, imp, outp = (os.path.join(tmp, n) for n in ("f16.gguf", "target.gguf", "imatrix.gguf",
+                                                                 "out.gguf"))
+        hdir = os.path.join(tmp, "hessians")
+        os.makedirs(hdir)
+        specs = [wl.spec_by_name[u.name] for u in wl.units]
+        xs = {wl.uid(u): wl.x[wl.uid(u)] for u in wl.units}
+        wf = GGUFWriter(f16p, "qwen3")
+        wt = GGUFWriter(tgtp, "qwen3")
+        for w_ in (wf, wt):
+            w_.add_uint32("qwen3.block_count", 28)
+            w_.add_string("general.name", "synthetic qwen3-0.6b-shaped")
+        for u, sp in zip(wl.units, specs):
+            x16 = xs[wl.uid(u)].to(torch.float16).cpu().numpy()
+            wf.add_tensor(sp.name, x16)
+            nb = kq.row_bytes(sp.ttype, sp.n)
+            wt.add_tensor(sp.name, np.zeros((sp.nrow, nb), np.uint8), raw_shape=(sp.nrow, nb),
+                          raw_dtype=getattr(gguf.GGMLQuantizationType, sp.ttype))
+        for w_ in (wf, wt):
+            w_.write_header_to_file()
+            w_.write_kv_data_to_file()
+            w_.write_tensors_to_file()
+            w_.close()
+        wi = GGUFWriter(imp, "imatrix")
+        for sp in specs:
+            if sp.mode == "EF":
+                wi.add_tensor(sp.name + ".in_sum2", (wl.diags[sp.hkey] * 1000.0).astype(np.float32))
+                wi.add_tensor(sp.name + ".counts", np.array([1000.0], np.float32))
+        wi.write_header_to_file()
+        wi.write_kv_data_to_file()
+        wi.write_tensors_to_file()
+        wi.close()
+        # one npz per tensor with a Hessian (q/k/v and gate/up hold the same matrix), written
+        # as the reference's collector writes them, on all host threads
+        host_h = {k: (wl.hess[k] * wl.tokens).float().cpu().numpy() for k in wl.hess}
+        todo = [(sp.name, host_h[sp.hkey]) for sp in specs if sp.mode == "EF"]
+        with cf.ThreadPoolExecutor(max_workers=cpu_threads()) as ex:
+            list(ex.map(lambda t: gguf_io.save_hessians({t[0]: {"H": t[1], "n": wl.tokens}}, hdir), todo))
+        del host_h
+        setup_s = time.perf_counter() - t0
+        sizes = {"f16_gguf_bytes": os.path.getsize(f16p), "target_gguf_bytes": os.path.getsize(tgtp),
+                 "hessian_npz_bytes": sum(os.path.getsize(os.path.join(hdir, f)) for f in os.listdir(hdir)),
+                 "hessian_files": len(os.listdir(hdir))}
+        quiet = lambda *_: None  # noqa: E731
+        ef.encode_gguf(f16p, tgtp, hdir, outp, imatrix_path=imp, log=quiet)
+        tm = {}
+        torch.cuda.synchronize()
+        st = ef.encode_gguf(f16p, tgtp, hdir, outp, imatrix_path=imp, log=quiet, timings=tm)
+        rec = {"seconds": tm["wall_s"], "value": wl.total_params / tm["wall_s"] / 1e6, "unit": UNIT,
+               "read_s": tm["read_s"], "device_s": tm["device_s"], "write_s": tm["write_s"],
+               "h2d_bytes": tm["h2d_bytes"], "d2h_bytes": tm["d2h_bytes"], "batches": tm["batches"],
+               "tensors": tm["tensors"], "out_gguf_bytes": os.path.getsize(outp), "setup_seconds": setup_s,
+               "page_cache": "warm (files written just before the runs)",
+               "path": "perm_b200.ef.encode_gguf: GGUF/npz read (reader thread) -> float16 weights and "
+                       "stored-form Hessians to the device -> decode, factor, EF encode -> GGUF re-emit",
+               "stats_median_rel_err_vs_stock": float(np.median([v["rel_err_vs_stock"] for v in st.values()]))}
+        rec.update(sizes)
+        return rec
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def measure_streamed(torch, dist, args, rank, world, local_rank):

@@ -151,6 +151,30 @@ def case_factor_model(torch, reps):
     return f"factor_model 112 Hessians: {dt * 1e3:.2f} ms, {fl / dt / 1e12:.2f} FP64 TFLOP/s"
 
 
+def case_factor_rank8(torch, reps):
+    """About one eighth of the 0.6B model's factorisations (3 at n = 3072, 4 at 2048, 7 at
+    1024): what one rank of an 8-GPU encode runs, bound by the length of the n = 3072 chain."""
+    from perm_b200.encoder import Encoder
+    hs = {}
+    for i in range(3):
+        hs[f"d{i}"] = _hess(torch, 3072, 30 + i)
+    for i in range(4):
+        hs[f"o{i}"] = _hess(torch, 2048, 20 + i)
+    for i in range(7):
+        hs[f"q{i}"] = _hess(torch, 1024, 10 + i)
+    ds = {k: torch.diagonal(v).cpu().numpy() for k, v in hs.items()}
+    enc = Encoder()
+    enc.factor(hs, ds)
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        enc.factor(hs, ds)
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t) / reps
+    fl = (2.0 / 3.0) * (3 * 3072 ** 3 + 4 * 2048 ** 3 + 7 * 1024 ** 3)
+    return f"factor_rank8 3x3072 + 4x2048 + 7x1024: {dt * 1e3:.2f} ms, {fl / dt / 1e12:.2f} FP64 TFLOP/s"
+
+
 def case_xtx(torch, reps, dtype="bf16"):
     from perm_b200 import hessians
     out = []
@@ -181,7 +205,7 @@ def case_xtx_f32(torch, reps):
     return case_xtx(torch, reps, "f32")
 
 
-CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
+CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "factor_rank8": case_factor_rank8, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):

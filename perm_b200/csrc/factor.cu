@@ -2,7 +2,10 @@
 // coldpress/ef.py:46-84 (cholesky_inv_upper) cast to float32, computed on the GPU as
 //     P  = J * Hd[order][:, order] * J          (act-order permutation, then reversal J)
 //     P  = L L^T                                (blocked left-looking Cholesky, nb = 64)
-//     U  = J * L^{-1} * J                       (blocked triangular inverse, then reversal)
+//     U  = J * L^{-1} * J                       (row-blocked triangular inverse, reversed)
+// The inverse runs as a second chain on a helper stream, one block row behind the
+// Cholesky: block row j of L^{-1} needs only block row j of L, the diagonal inverses and the
+// earlier rows of L^{-1}, so the two dependent chains overlap instead of following each other.
 // Because Hd = (J L J)(J L J)^T with J L J upper, (J L^{-1} J) is the unique upper factor
 // with U^T U = inv(Hd): the same matrix as the reference's inv-then-cholesky route, in one
 // Cholesky plus one triangular inverse.  Every step stays in float64 so the float32 cast
@@ -10,6 +13,8 @@
 // then escalates the damping exactly like the reference does.
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <map>
+#include <utility>
 #include "ef_kernels.h"
 #include "kquant_kernels.h"
 
@@ -37,8 +42,12 @@ static int ksplit_batch(int K, int tiles, int count) {
   const int s = (int)((slots + base - 1) / base);
   return s < smax ? s : smax;
 }
-// partial tiles live after P (n x n) and T (n x 64) in each item's workspace
-__device__ __forceinline__ double* part_base(double* P, int n) { return P + (size_t)n * n + (size_t)n * NB; }
+// Workspace of one item: P (n x n), T (n x 64: a 64 x 64 scratch tile per block column),
+// D (n x 64: the transposed inverse of each 64 x 64 diagonal block of L), then the split-K
+// partial tiles (kSplitMax x n x 64).
+__device__ __forceinline__ double* t_base(double* P, int n) { return P + (size_t)n * n; }
+__device__ __forceinline__ double* d_base(double* P, int n) { return P + (size_t)n * n + (size_t)n * NB; }
+__device__ __forceinline__ double* part_base(double* P, int n) { return P + (size_t)n * n + 2 * (size_t)n * NB; }
 
 // P[i][j] = H[order[n-1-i]][order[n-1-j]] (+ shift on the diagonal).  Only the lower
 // triangle is consumed; the strict upper triangle is written as zero.  blockIdx.z: item.
@@ -246,6 +255,20 @@ __global__ void __launch_bounds__(256) potrf_inv_diag_kernel(const __grid_consta
     const int r = i >> 6, c = i & 63;
     A[(size_t)(k + r) * n + k + c] = (c <= r) ? x[r][c] : 0.0;
   }
+  // the inverse chain reads this block transposed: D_k[c][r] = inv(L_kk)[r][c] (zero for r < c)
+  double* __restrict__ Dk = d_base(A, n) + (size_t)k * 64;
+  for (int i = t; i < 64 * 64; i += 256) {
+    const int c = i >> 6, r = i & 63;
+    Dk[i] = (r >= c) ? x[r][c] : 0.0;
+  }
+  // U's diagonal block: U[n-1-(k+r)][n-1-(k+c)] = inv(L_kk)[r][c] for c <= r
+  for (int i = t; i < 64 * 64; i += 256) {
+    const int r = i >> 6, c = i & 63;
+    if (c > r) continue;
+    const size_t u = (size_t)(n - 1 - (k + r)) * n + (size_t)(n - 1 - (k + c));
+    if (fb.out_f64) static_cast<double*>(fb.U[blockIdx.x])[u] = x[r][c];
+    else static_cast<float*>(fb.U[blockIdx.x])[u] = (float)x[r][c];
+  }
 }
 
 __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool ok) {
@@ -279,17 +302,20 @@ __device__ __forceinline__ void mma_f64(double (&d)[4], const double (&a)[8], co
 
 template <bool B_NK>
 __device__ __forceinline__ void tile64(const double* __restrict__ A, int lda, const double* __restrict__ B, int ldb,
-                                       int m_lim, int n_lim, int k_len, double (&acc)[2][4][4]) {
+                                       int m_lim, int n_lim, int k_len, double (&acc)[2][4][4],
+                                       bool accumulate = false) {
   __shared__ __align__(16) double sa[2][64 * kAP];
   __shared__ __align__(16) double sb[2][B_NK ? 64 * kAP : 16 * kBP];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5, g = lane >> 2, q = lane & 3;
   const int wm = 32 * (warp >> 1), wn = 32 * (warp & 1);
+  if (!accumulate) {
 #pragma unroll
-  for (int i = 0; i < 2; i++)
+    for (int i = 0; i < 2; i++)
 #pragma unroll
-    for (int j = 0; j < 4; j++)
+      for (int j = 0; j < 4; j++)
 #pragma unroll
-      for (int v = 0; v < 4; v++) acc[i][j][v] = 0.0;
+        for (int v = 0; v < 4; v++) acc[i][j][v] = 0.0;
+  }
   auto load = [&](int l0, int buf) {
 #pragma unroll
     for (int k = 0; k < 512 / kFT; k++) {  // A chunk: 64 rows x 16 doubles = 512 x 16 bytes
@@ -401,25 +427,6 @@ __global__ void __launch_bounds__(256) chol_reduce_kernel(const __grid_constant_
   }
 }
 
-// Split-K reduction of a triangular-inverse step: T rows = -(part_0 + ... + part_{S-1}).
-__global__ void __launch_bounds__(256) trinv_reduce_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
-  const int n = fb.n;
-  double* __restrict__ Pw = fb.P[blockIdx.y];
-  double* __restrict__ T = Pw + (size_t)n * n;
-  if (*fb.status[blockIdx.y]) return;
-  const double* part = part_base(Pw, n);
-  const int base = j + NB;
-  const int r0 = base + blockIdx.x * 64;
-  const int m = min(64, n - r0);
-  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
-    const int rr = i / 64, c = i % 64;
-    if (rr >= m) continue;
-    double v = 0.0;
-    for (int q = 0; q < S; q++) v += part[((size_t)q * n + r0 - base + rr) * NB + c];
-    T[(size_t)(r0 - base + rr) * NB + c] = -v;
-  }
-}
-
 // Panel below the diagonal block: A[j+64:n, j:j+64] := A * inv(L_jj)^T (inverse on the diagonal).
 __global__ void __launch_bounds__(kFT) trsm_panel_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
@@ -435,82 +442,92 @@ __global__ void __launch_bounds__(kFT) trsm_panel_kernel(const __grid_constant__
   });
 }
 
-// Triangular inverse, step for diagonal block j (blocks to its lower right already inverted):
-//   T = -Linv22 * L21          (rows below, into scratch; Linv22 is lower triangular)
-// With S > 1 the K range is split over blockIdx.y; partial products go to the partial-tile
-// scratch and trinv_reduce_kernel forms T from them in order.
-__global__ void __launch_bounds__(kFT) trmm_kernel(const __grid_constant__ FactorBatch fb, int j, int S) {
+// Triangular inverse, block row j (a chain on the helper stream, started once the Cholesky
+// chain has inverted the diagonal block j):
+//   Linv[jb, c] = -inv(L_jj) * (L[jb, c] inv(L_cc) + sum_{c < k < j} L[jb, k] Linv[k, c])
+// for every 64-column tile c < j, where jb is block row j.  Block row j of L is final (the
+// Cholesky chain no longer touches it), the diagonal inverses come transposed from D, and the
+// off-diagonal blocks of Linv are kept transposed in the strict upper triangle of P, which
+// the Cholesky chain never reads.  Each result also goes straight to U (reversed, cast).
+// One CTA per (column tile, item); T holds each tile's intermediate product.
+__global__ void __launch_bounds__(kFT) trinv_row_kernel(const __grid_constant__ FactorBatch fb, int j) {
   const int n = fb.n;
-  double* __restrict__ Pw = fb.P[blockIdx.z];
-  const double* __restrict__ A = Pw;
-  double* __restrict__ T = Pw + (size_t)n * n;
-  if (*fb.status[blockIdx.z]) return;
-  const int base = j + NB;
-  const int r0 = base + blockIdx.x * 64;
-  const int m = min(64, n - r0);
-  const int k_len = r0 + m - base;  // rows r0.. of Linv22 vanish right of column r0+m-1
-  const int q = blockIdx.y, chunk = kchunk(n - base, S);
-  const int k0 = q * chunk, k1 = min(k_len, k0 + chunk);
-  double acc[2][4][4];
-  tile64<false>(A + (size_t)r0 * n + base + k0, n, A + (size_t)(base + k0) * n + j, n, m, 64, k1 - k0, acc);
-  double* part = part_base(Pw, n) + (size_t)q * n * NB;
-  tile_for_each(acc, [&](int r, int c, double v) {
-    if (r >= m) return;
-    if (S == 1) T[(size_t)(r0 - base + r) * NB + c] = -v;
-    else part[(size_t)(r0 - base + r) * NB + c] = v;
-  });
-}
-
-//   L21 := T * inv(L_jj)   (inv(L_jj) already sits on the diagonal)
-__global__ void __launch_bounds__(kFT) trinv_apply_kernel(const __grid_constant__ FactorBatch fb, int j) {
-  const int n = fb.n;
-  double* __restrict__ A = fb.P[blockIdx.y];
-  double* __restrict__ T = fb.P[blockIdx.y] + (size_t)n * n;
+  double* __restrict__ P = fb.P[blockIdx.y];
   if (*fb.status[blockIdx.y]) return;
-  const int base = j + NB;
-  const int r0 = base + blockIdx.x * 64;
-  const int m = min(64, n - r0);
+  const int c0 = blockIdx.x * 64;
+  double* __restrict__ S = t_base(P, n) + (size_t)c0 * 64;   // S[c][r] = product[r][c]
   double acc[2][4][4];
-  tile64<false>(T + (size_t)(r0 - base) * NB, NB, A + (size_t)j * n + j, n, m, 64, 64, acc);
+  tile64<true>(P + (size_t)j * n + c0, n, d_base(P, n) + (size_t)c0 * 64, 64, 64, 64, 64, acc, false);
+  if (j - c0 - 64 > 0)
+    tile64<true>(P + (size_t)j * n + c0 + 64, n, P + (size_t)c0 * n + c0 + 64, n, 64, 64, j - c0 - 64, acc, true);
+  tile_for_each(acc, [&](int r, int c, double v) { S[(size_t)c * 64 + r] = v; });
+  __threadfence_block();
+  __syncthreads();
+  tile64<true>(P + (size_t)j * n + j, n, S, 64, 64, 64, 64, acc, false);
   tile_for_each(acc, [&](int r, int c, double v) {
-    if (r < m) A[(size_t)(r0 + r) * n + j + c] = v;
+    P[(size_t)(c0 + c) * n + j + r] = -v;
+    const size_t u = (size_t)(n - 1 - (j + r)) * n + (size_t)(n - 1 - (c0 + c));
+    if (fb.out_f64) static_cast<double*>(fb.U[blockIdx.y])[u] = -v;
+    else static_cast<float*>(fb.U[blockIdx.y])[u] = (float)(-v);
   });
-}
-
-// U[i][j] = Linv[n-1-i][n-1-j] for j >= i, else 0 (cast to OutT).
-template <typename OutT>
-__global__ void unreverse_cast_kernel(const __grid_constant__ FactorBatch fb) {
-  const int n = fb.n;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
-  if (j >= n) return;
-  const double* __restrict__ Linv = fb.P[blockIdx.z];
-  OutT* __restrict__ U = (OutT*)fb.U[blockIdx.z];
-  U[(size_t)i * n + j] = (j >= i) ? (OutT)Linv[(size_t)(n - 1 - i) * n + (n - 1 - j)] : (OutT)0;
 }
 
 size_t factor_workspace_bytes(int64_t n) {
-  // P (n x n f64) + T (n x nb) + split-K partial tiles (kSplitMax x n x nb)
-  return ((size_t)n * n + (size_t)n * NB + (size_t)kSplitMax * n * NB) * sizeof(double);
+  // P (n x n f64) + T and D (n x nb each) + split-K partial tiles (kSplitMax x n x nb)
+  return ((size_t)n * n + 2 * (size_t)n * NB + (size_t)kSplitMax * n * NB) * sizeof(double);
 }
+
+namespace {
+// The inverse chain's stream: one per (host thread, device, caller stream), created on first
+// use with the caller stream's priority, plus the events that fork it from the caller, hand
+// it each inverted diagonal block and join it back.
+struct InvHelper {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, step = nullptr, join = nullptr;
+};
+int inv_helper(cudaStream_t caller, InvHelper** out) {
+  static thread_local std::map<std::pair<int, cudaStream_t>, InvHelper> helpers;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+  InvHelper& h = helpers[std::make_pair(dev, caller)];
+  if (!h.s) {
+    int prio = 0;
+    if (cudaStreamGetPriority(caller, &prio) != cudaSuccess) prio = 0;
+    if (cudaStreamCreateWithPriority(&h.s, cudaStreamNonBlocking, prio) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h.step, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h.join, cudaEventDisableTiming) != cudaSuccess)
+      return 1;
+  }
+  *out = &h;
+  return 0;
+}
+}  // namespace
 
 int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
   const int n = fb.n, cnt = fb.count;
   if (cnt <= 0) return 0;
   if (n <= 0 || n % NB) return 2;
   {  // the diagonal-block and row-staged permute kernels use more than the 48 KB default (per device)
-    static unsigned long long opted = 0;
+    static std::atomic<unsigned long long> opted{0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
-    if (!(opted & (1ULL << dev))) {
+    if (!(opted.load() & (1ULL << dev))) {
       if (cudaFuncSetAttribute(potrf_inv_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kPotrfSmemBytes) != cudaSuccess ||
           cudaFuncSetAttribute(permute_reverse_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kPermRowSmemMax) != cudaSuccess)
         return 1;
-      opted |= 1ULL << dev;
+      opted.fetch_or(1ULL << dev);
     }
   }
-  for (int b = 0; b < cnt; b++) cudaMemsetAsync(fb.status[b], 0, sizeof(int), stream);
+  InvHelper* hp = nullptr;
+  if (inv_helper(stream, &hp)) return 1;
+  const size_t ubytes = (size_t)n * n * (fb.out_f64 ? sizeof(double) : sizeof(float));
+  for (int b = 0; b < cnt; b++) {
+    cudaMemsetAsync(fb.status[b], 0, sizeof(int), stream);
+    cudaMemsetAsync(fb.U[b], 0, ubytes, stream);   // U's strict lower triangle stays zero
+  }
   if ((size_t)n * sizeof(double) <= (size_t)kPermRowSmemMax) {
     permute_reverse_rows_kernel<<<dim3((unsigned)n, (unsigned)cnt), 256, (size_t)n * sizeof(double), stream>>>(fb);
     note_launch();
@@ -519,6 +536,8 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     permute_reverse_kernel<<<g, 256, 0, stream>>>(fb);
     note_launch();
   }
+  cudaEventRecord(hp->fork, stream);
+  cudaStreamWaitEvent(hp->s, hp->fork, 0);
   for (int j = 0; j < n; j += NB) {
     const int S = j > 0 ? ksplit_batch(j, (n - j) / 64, cnt) : 1;
     if (j > 0) {
@@ -531,31 +550,19 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     }
     potrf_inv_diag_kernel<<<(unsigned)cnt, 256, kPotrfSmemBytes, stream>>>(fb, j);
     note_launch();
+    if (j > 0) {   // block row j of the inverse, on the helper stream
+      cudaEventRecord(hp->step, stream);
+      cudaStreamWaitEvent(hp->s, hp->step, 0);
+      trinv_row_kernel<<<dim3((unsigned)(j / 64), (unsigned)cnt), kFT, 0, hp->s>>>(fb, j);
+      note_launch();
+    }
     if (n - j - NB > 0) {
       trsm_panel_kernel<<<dim3((unsigned)((n - j - NB) / 64), (unsigned)cnt), kFT, 0, stream>>>(fb, j);
       note_launch();
     }
   }
-  // blocked inverse of L, bottom-right to top-left (LAPACK dtrtri, lower); the diagonal
-  // blocks were inverted by the factorisation
-  for (int j = n - 2 * NB; j >= 0; j -= NB) {
-    const unsigned tiles = (unsigned)((n - j - NB + 63) / 64);
-    const int S = ksplit_batch(n - j - NB, (int)tiles, cnt);
-    trmm_kernel<<<dim3(tiles, (unsigned)S, (unsigned)cnt), kFT, 0, stream>>>(fb, j, S);
-    note_launch();
-    if (S > 1) {
-      trinv_reduce_kernel<<<dim3(tiles, (unsigned)cnt), 256, 0, stream>>>(fb, j, S);
-      note_launch();
-    }
-    trinv_apply_kernel<<<dim3(tiles, (unsigned)cnt), kFT, 0, stream>>>(fb, j);
-    note_launch();
-  }
-  {
-    dim3 g((unsigned)((n + 255) / 256), (unsigned)n, (unsigned)cnt);
-    if (fb.out_f64) unreverse_cast_kernel<double><<<g, 256, 0, stream>>>(fb);
-    else unreverse_cast_kernel<float><<<g, 256, 0, stream>>>(fb);
-    note_launch();
-  }
+  cudaEventRecord(hp->join, hp->s);
+  cudaStreamWaitEvent(stream, hp->join, 0);
   return 0;
 }
 

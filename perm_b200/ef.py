@@ -164,20 +164,31 @@ def _hessian_to_device(torch, st, perm=None):
 
 def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, perms=None, spacemap=None, dims=None,
                 acknowledge_unreviewed=False, only="all", n_iter=2, unsafe_storage_order=False, device="cuda",
-                log=print, max_params_per_batch=2_000_000_000):
+                log=print, max_params_per_batch=200_000_000, timings=None):
     """ef.py:223-317 on the GPU: EF-encode every quantized tensor of `target_path` with the f16
     weights of `f16_path` and the Hessians in `hessdir`, write a clone of the target with the
     new payloads to `out_path` and the per-tensor statistics to out_path + ".efstats.json".
 
     Same arguments, modes ("EF", "wRTN(attn0-diag)" for token_embd, "wRTN" without a
-    Hessian), errors and outputs as the reference; tensors are encoded in device batches of
-    at most max_params_per_batch parameters and identical Hessians are factorised once."""
+    Hessian), errors and outputs as the reference; identical Hessians are factorised once.
+    Tensors go through the device in batches of at most max_params_per_batch parameters
+    (Encoder.run_stream, one batch in flight ahead of the host), and the file work overlaps the
+    device work: a reader thread loads the next batch's weights and Hessian files (npz
+    decompression) while the device encodes the current one; the float16 weights and the
+    stored-form Hessians (float16 / hscale + float32 diagonal) travel to the device in that
+    form on a copy stream and are widened / decoded there; the packed bytes come back on
+    their own stream as each batch finishes.  timings (a dict, optional) receives the wall
+    time and its parts: read_s (reader thread), device_s (from the first batch queued to the
+    last batch finished), write_s (the GGUF re-emit), bytes moved each way."""
+    import concurrent.futures as cf
     import hashlib
     import json
+    import os
     import time
     from gguf import GGUFReader
     from . import gguf_io
-    from .encoder import Encoder, Job
+    from .encoder import Encoder, Job, StreamBatch
+    t_start = time.time()
     if device is not None and not str(device).startswith("cuda"):
         raise ValueError(f"perm_b200.encode_gguf runs on CUDA devices only (device={device!r})")
     imat = gguf_io.imatrix_means(imatrix_path) if imatrix_path else {}
@@ -221,54 +232,189 @@ def encode_gguf(f16_path, target_path, hessdir, out_path, imatrix_path=None, per
         else:
             plan.append((name, tt, "wRTN", qw, None, None, p))
 
-    enc = Encoder(n_iter=n_iter, act_order=not unsafe_storage_order)
-    replace, stats = {}, {}
-    t_start = time.time()
-    i = 0
-    while i < len(plan):
-        batch, total = [], 0
-        while i < len(plan) and (not batch or total + f16[plan[i][0]].n_elements <= max_params_per_batch):
-            batch.append(plan[i])
-            total += int(f16[plan[i][0]].n_elements)
-            i += 1
+    batches, cur, total = [], [], 0
+    for item in plan:
+        ne = int(f16[item[0]].n_elements)
+        if cur and total + ne > max_params_per_batch:
+            batches.append(cur)
+            cur, total = [], 0
+        cur.append(item)
+        total += ne
+    if cur:
+        batches.append(cur)
+
+    clock = {"read_s": 0.0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    def read_weight(name):
+        a = np.asarray(f16[name].data)
+        if a.dtype == np.float16:
+            host = torch.empty(a.shape, dtype=torch.float16, pin_memory=True)
+            host.numpy()[...] = a
+        else:
+            host = torch.empty(a.shape, dtype=torch.float32, pin_memory=True)
+            host.numpy()[...] = a.astype(np.float32)
+        return host
+
+    def read_hessian(item):
+        name, tt, mode, qw, hname, fit_w, p = item
+        st = gguf_io.load_hessian_stored(hessdir, hname)   # npz decompression: releases the GIL
+        dig = hashlib.sha1(st["h"].tobytes())
+        dig.update(np.float64(st["hscale"]).tobytes())
+        if st["diag32"] is not None:
+            dig.update(st["diag32"].tobytes())
+        if p is not None:
+            dig.update(np.asarray(p, np.int64).tobytes())
+        return dig.hexdigest(), st
+
+    def read_batch(batch):
+        """Reader thread: the batch's weights (float16 when the source holds float16) and its
+        stored Hessians with a content digest each, in pinned host memory; the files of a
+        batch are read and decompressed by a pool of host threads."""
         t0 = time.time()
-        hess_dev, hkey_of, diags = {}, {}, {}
-        jobs = []
-        for name, tt, mode, qw, hname, fit_w, p in batch:
-            x = torch.from_numpy(np.ascontiguousarray(np.asarray(f16[name].data).astype(np.float32))).cuda()
-            hk = None
-            if hname is not None:
-                st = gguf_io.load_hessian_stored(hessdir, hname)
-                dig = hashlib.sha1(st["h"].tobytes())
-                dig.update(np.float64(st["hscale"]).tobytes())
-                if st["diag32"] is not None:
-                    dig.update(st["diag32"].tobytes())
-                if p is not None:
-                    dig.update(np.asarray(p, np.int64).tobytes())
-                hk = dig.hexdigest()
-                if hk not in hess_dev:
-                    hess_dev[hk] = _hessian_to_device(torch, st, p)
-                    diags[hk] = torch.diagonal(hess_dev[hk]).cpu().numpy()
-            jobs.append(Job(name, tt, "EF" if mode.startswith("EF") else mode, x,
-                            None if qw is None else torch.from_numpy(kq.host_array(qw, np.float32)).cuda(),
-                            hk, None if fit_w is None else torch.from_numpy(fit_w).cuda()))
-        raws, st = enc.run(jobs, hess_dev, diags, stats=True)
-        dt = time.time() - t0
-        for (name, tt, mode, *_), j in zip(batch, jobs):
-            replace[name] = raws[name].cpu().numpy().reshape(-1)
-            s = st[name]
-            s["mode"] = mode
-            s["sec"] = dt * j.params / max(1, total)
-            stats[name] = s
-        for k, (name, tt, mode, *_) in enumerate(batch):
-            if (len(stats) - len(batch) + k + 1) % 20 == 0 or name in ("token_embd.weight", "output.weight"):
-                log(f"[{len(stats) - len(batch) + k + 1}/{len(targets)}] {name} {tt} {mode} "
-                    f"err-vs-stock {stats[name]['rel_err_vs_stock'] * 100:+.1f}% ({stats[name]['sec']:.1f}s)")
-        del jobs, raws, hess_dev
+        w = dict(zip([it[0] for it in batch], io.map(read_weight, [it[0] for it in batch])))
+        items = [it for it in batch if it[4] is not None]
+        hs, pinned = {}, set()
+        for it, (key, st) in zip(items, io.map(read_hessian, items)):
+            if it[6] is None and st["h"].dtype == np.float16 and key not in pinned:
+                st["h_pinned"] = torch.from_numpy(np.ascontiguousarray(st["h"]).view(np.int16)).pin_memory()
+                pinned.add(key)
+            hs[it[0]] = (key, st)
+        clock["read_s"] += time.time() - t0
+        return w, hs
+
+    enc = Encoder(n_iter=n_iter, act_order=not unsafe_storage_order)
+    copy_s = torch.cuda.Stream()               # host -> device, in order
+    work_s = torch.cuda.Stream(priority=-1)    # widening and Hessian decodes, ahead of the fits
+    d2h_s = torch.cuda.Stream()
+    main = torch.cuda.current_stream()
+    pool = cf.ThreadPoolExecutor(max_workers=1)        # reads the next batch ahead
+    io = cf.ThreadPoolExecutor(max_workers=max(1, min(16, os.cpu_count() or 1)))   # its files
+
+    def stream_batches():
+        fut = pool.submit(read_batch, batches[0])
+        for bi, batch in enumerate(batches):
+            w_host, hs_host = fut.result()
+            if bi + 1 < len(batches):
+                fut = pool.submit(read_batch, batches[bi + 1])
+            t_draw = time.time()
+            hess_dev, diags, ready, jobs, keep = {}, {}, {}, [], [w_host, hs_host]
+            by_key = {}
+            for name, (key, st) in hs_host.items():
+                if key in by_key:
+                    continue
+                by_key[key] = st
+                d = st["h"].shape[0]
+                if "h_pinned" in st:
+                    with torch.cuda.stream(copy_s):
+                        h16 = torch.empty((d, d), dtype=torch.int16, device="cuda")
+                        h16.copy_(st["h_pinned"], non_blocking=True)
+                        d32 = None
+                        if st["diag32"] is not None:
+                            d32h = torch.from_numpy(st["diag32"]).pin_memory()
+                            d32 = torch.empty(d, dtype=torch.float32, device="cuda")
+                            d32.copy_(d32h, non_blocking=True)
+                            keep.append(d32h)
+                    arrived = torch.cuda.Event()
+                    arrived.record(copy_s)
+                    work_s.wait_event(arrived)
+                    with torch.cuda.stream(work_s):
+                        H = torch.empty((d, d), dtype=torch.float64, device="cuda")
+                    nat.check(nat.lib().cp_hessian_decode(nat.ptr(h16), nat.ptr(d32), float(st["hscale"]), d,
+                                                          nat.ptr(H), nat.stream_ptr(torch, work_s)), "hessian_decode")
+                    for t_ in (h16, d32):
+                        if t_ is not None:
+                            t_.record_stream(work_s)
+                    ev = torch.cuda.Event()
+                    ev.record(work_s)
+                    ready[d] = ev            # the last decode of this size so far
+                    clock["h2d_bytes"] += d * d * 2 + (d * 4 if d32 is not None else 0)
+                else:   # permuted or float32-stored Hessians: decoded on the host
+                    p = next(item[6] for item in batch if item[4] is not None and hs_host[item[0]][0] == key)
+                    H = _hessian_to_device(torch, st, p)
+                    clock["h2d_bytes"] += H.numel() * 8
+                hess_dev[key] = H
+                if "h_pinned" in st:   # the decode's own diagonal, computed on the host
+                    diags[key] = (st["diag32"].astype(np.float64) if st["diag32"] is not None else
+                                  st["h"].diagonal().astype(np.float64) * float(st["hscale"]))
+                else:
+                    diags[key] = torch.diagonal(H).cpu().numpy()
+            staged = []
+
+            def upload_small(a):   # imatrix means / fit weights: pinned, on the copy stream
+                if a is None:
+                    return None
+                h = torch.from_numpy(kq.host_array(a, np.float32)).pin_memory()
+                with torch.cuda.stream(copy_s):
+                    dv = torch.empty(h.shape, dtype=torch.float32, device="cuda")
+                    dv.copy_(h, non_blocking=True)
+                dv.record_stream(main)
+                keep.append(h)
+                return dv
+
+            for name, tt, mode, qw, hname, fit_w, p in batch:
+                host = w_host[name]
+                qw_dev, fw_dev = upload_small(qw), upload_small(fit_w)
+                with torch.cuda.stream(copy_s):
+                    dev = torch.empty(host.shape, dtype=host.dtype, device="cuda")
+                    dev.copy_(host, non_blocking=True)
+                clock["h2d_bytes"] += host.numel() * host.element_size()
+                arrived = torch.cuda.Event()
+                arrived.record(copy_s)
+                work_s.wait_event(arrived)
+                with torch.cuda.stream(work_s):
+                    x = dev.float() if dev.dtype != torch.float32 else dev
+                dev.record_stream(work_s)
+                x.record_stream(main)
+                ev = torch.cuda.Event()
+                ev.record(work_s)
+                staged.append((ev, [name]))
+                jobs.append(Job(name, tt, "EF" if mode.startswith("EF") else mode, x, qw_dev,
+                                hs_host[name][0] if hname is not None else None, fw_dev))
+            yield StreamBatch(jobs, hess_dev, diags, None, staged, ready, tag=(batch, t_draw, keep))
+
+    replace, stats, pending = {}, {}, []
+    t_last = [time.time()]
+
+    def on_batch(b, raws, st):
+        batch, t_draw, _keep = b.tag
+        now = time.time()
+        dt = now - max(t_draw, t_last[0])
+        t_last[0] = now
+        tot = sum(j.params for j in b.jobs) or 1
+        for (name, tt, mode, *_), j in zip(batch, b.jobs):
+            host = torch.empty(raws[name].shape, dtype=torch.uint8, pin_memory=True)
+            with torch.cuda.stream(d2h_s):
+                host.copy_(raws[name], non_blocking=True)
+            clock["d2h_bytes"] += host.numel()
+            pending.append((name, host, raws[name]))
+            s_ = {"type": st[name]["type"], "mode": mode, "rel_err_vs_stock": st[name]["rel_err_vs_stock"],
+                  "sec": dt * j.params / tot}
+            stats[name] = s_
+            k = len(stats)
+            if k % 20 == 0 or name in ("token_embd.weight", "output.weight"):
+                log(f"[{k}/{len(targets)}] {name} {tt} {mode} "
+                    f"err-vs-stock {s_['rel_err_vs_stock'] * 100:+.1f}% ({s_['sec']:.1f}s)")
+
+    t_dev = time.time()
+    if batches:
+        enc.run_stream(stream_batches(), stats=True, on_batch=on_batch)
+    d2h_s.synchronize()
+    pool.shutdown()
+    io.shutdown()
+    device_s = time.time() - t_dev
+    for name, host, _dev in pending:
+        replace[name] = host.numpy().reshape(-1)
+    t_w = time.time()
     gguf_io.copy_gguf(target_path, out_path, replace)
-    if stats:
-        med = float(np.median([s["rel_err_vs_stock"] for s in stats.values()]))
+    write_s = time.time() - t_w
+    ordered = {name: stats[name] for name, *_ in plan if name in stats}
+    if ordered:
+        med = float(np.median([s["rel_err_vs_stock"] for s in ordered.values()]))
         log(f"median err-vs-stock: {med * 100:+.2f}%; total {(time.time() - t_start) / 60:.1f} min")
     with open(out_path + ".efstats.json", "w") as fh:
-        json.dump(stats, fh, indent=1)
-    return stats
+        json.dump(ordered, fh, indent=1)
+    if timings is not None:
+        timings.update({"wall_s": time.time() - t_start, "read_s": clock["read_s"], "device_s": device_s,
+                        "write_s": write_s, "h2d_bytes": clock["h2d_bytes"], "d2h_bytes": clock["d2h_bytes"],
+                        "batches": len(batches), "tensors": len(ordered)})
+    return ordered

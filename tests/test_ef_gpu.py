@@ -100,6 +100,8 @@ def test_ef_config0_matches_oracle(ef, orc):
     assert abs(rel) <= HERR_GATE, f"H-weighted error differs by {rel * 100:.4f}%"
     print(f"config0 EF: codes identical {frac * 100:.4f}%, bytes identical "
           f"{np.mean(raw == oraw) * 100:.4f}%, H-err rel {rel * 100:+.5f}%")
+    # beyond the gates: the ordered sweep and the FP64 factor reproduce the bytes exactly
+    assert np.array_equal(raw, oraw), f"{np.count_nonzero(raw != oraw)} bytes differ"
 
 
 @pytest.mark.parametrize("tt", ["Q3_K", "Q6_K", "Q4_K"])

@@ -49,3 +49,34 @@ def test_encode_gguf_matches_reference_semantics(tmp_path, orc):
     assert all(np.isfinite(v["rel_err_vs_stock"]) for v in on_disk.values())
 
 
+
+
+def test_encode_gguf_batches_and_timings(tmp_path, orc):
+    """Small batches (several in flight through Encoder.run_stream, each tensor's inputs
+    uploaded in storage form and decoded on the device) give exactly the bytes and statistics
+    of one batch, and the timings record is filled."""
+    from gguf import GGUFReader
+    from perm_b200 import ef, gguf_io
+    W = fx.weights()
+    f16, tgt = str(tmp_path / "f16.gguf"), str(tmp_path / "t.gguf")
+    hdir, imp = str(tmp_path / "hess"), str(tmp_path / "im.gguf")
+    fx.write_f16(f16, W)
+    fx.write_target(tgt, W, orc.quantize)
+    gguf_io.save_hessians(fx.hessians(), hdir)
+    fx.write_imatrix(imp, [(n, ne0) for n, tt, ne0, nrow in fx.SPEC if n != "token_embd.weight"])
+    one, many = str(tmp_path / "one.gguf"), str(tmp_path / "many.gguf")
+    st1 = ef.encode_gguf(f16, tgt, hdir, one, imatrix_path=imp, log=lambda *_: None)
+    tm = {}
+    st2 = ef.encode_gguf(f16, tgt, hdir, many, imatrix_path=imp, log=lambda *_: None, max_params_per_batch=100_000,
+                         timings=tm)
+    a = {t.name: np.asarray(t.data) for t in GGUFReader(one).tensors}
+    b = {t.name: np.asarray(t.data) for t in GGUFReader(many).tensors}
+    assert a.keys() == b.keys()
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+    assert list(st1) == list(st2) == [n for n, *_ in fx.SPEC]
+    for k in st1:
+        assert st1[k]["rel_err_vs_stock"] == pytest.approx(st2[k]["rel_err_vs_stock"], rel=1e-9, abs=1e-12)
+        assert set(st1[k]) == {"type", "mode", "rel_err_vs_stock", "sec"}
+    assert tm["batches"] >= 4 and tm["tensors"] == len(fx.SPEC)
+    assert tm["h2d_bytes"] > 0 and tm["d2h_bytes"] > 0 and tm["wall_s"] >= tm["write_s"]

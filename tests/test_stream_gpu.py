@@ -65,7 +65,9 @@ def test_stream_matches_one_pass():
     for j in jobs:
         a, b = got[j.name].cpu().numpy(), want[j.name].cpu().numpy()
         assert np.array_equal(a, b), f"{j.name}: {np.count_nonzero(a != b)} bytes differ"
-        assert st_got[j.name]["rel_err_vs_stock"] == st_want[j.name]["rel_err_vs_stock"]
+        # the statistics' float64 sums are reduced with atomics: equal up to summation order
+        assert st_got[j.name]["rel_err_vs_stock"] == pytest.approx(st_want[j.name]["rel_err_vs_stock"],
+                                                                   rel=1e-9, abs=1e-12)
 
 
 def test_stream_escalates_inside_a_batch(orc):
