@@ -52,6 +52,7 @@ def parse():
     # the second workload of the line: the Llama-3-8B-shaped Q4_K_M-style encode (BASELINE
     # config[4]), streamed through the device in batches of layers
     ap.add_argument("--no-gguf", action="store_true")
+    ap.add_argument("--no-config2", action="store_true")
     ap.add_argument("--no-config4", action="store_true")
     ap.add_argument("--config4-model", default="llama3-8b")
     ap.add_argument("--config4-mixture", default="q4_k_m_style")
@@ -266,6 +267,58 @@ def run_cpu_baseline(seed, reps=1):
             "sample": "layer 0 of the Qwen3-0.6B-shaped model (7 tensors, 25.2 M params): EF n_iter 2 "
                       "(numpy LAPACK factor + C oracle fits/sweeps) plus the stock-baseline roundtrip, "
                       "H from 8192 tokens", "seconds": dt}
+
+
+def run_cpu_baseline_on_workload(torch, wl, outputs, rows_big=64):
+    """The CPU port timed on a bounded sample of the GPU workload itself, which doubles as the
+    bench's parity check: layer 0's seven tensors (the timed sample) plus the first rows of
+    output.weight and token_embd.weight, with the same weights and Hessians as the device run,
+    encoded by the CPU oracle (a restatement of ef.py / kquant.py) and compared byte for byte
+    with the packed bytes the last timed step left on the device (rows are independent, so a
+    row slice of a tensor encodes to the same bytes as those rows of the whole tensor)."""
+    from oracle import oracle as orc
+    orc.build()
+    nt = cpu_threads()
+    items = []
+    for u in wl.units:
+        sp = wl.spec_by_name[u.name]
+        if sp.name.startswith("blk.0."):
+            items.append((u, sp, slice(0, u.r1 - u.r0), True))
+        elif sp.name in ("output.weight", "token_embd.weight"):
+            items.append((u, sp, slice(0, min(rows_big, u.r1 - u.r0)), False))
+    host_h = {}
+    n_params, dt = 0, 0.0
+    checked, same_bytes, min_codes = 0, 0, 1.0
+    for u, sp, rs, timed in items:
+        uid = wl.uid(u)
+        W = wl.x[uid][rs].cpu().numpy()
+        if sp.hkey not in host_h:
+            host_h[sp.hkey] = wl.hess[sp.hkey].cpu().numpy()
+        H = host_h[sp.hkey]
+        qw = wl.diags[sp.hkey].astype(np.float32)
+        t0 = time.perf_counter()
+        if sp.mode == "EF":
+            want, _ = orc.ef_encode(W, sp.ttype, qw, H, n_iter=2, act_order=True, nthreads=nt)
+            orc.roundtrip(W, sp.ttype, qw)   # the statistics' stock baseline (ef.py:298)
+        else:   # token_embd: weighted RTN with the attn0 diagonal (ef.py:280-285), plus its baseline
+            want = orc.quantize(sp.ttype, W, qw, nt)
+            orc.roundtrip(W, sp.ttype, None)
+        if timed:
+            dt += time.perf_counter() - t0
+            n_params += W.size
+        got = outputs[uid][rs].cpu().numpy()
+        checked += 1
+        same_bytes += int(np.array_equal(got, want))
+        codes = float(np.mean(orc.codes(sp.ttype, got, *W.shape) == orc.codes(sp.ttype, want, *W.shape)))
+        min_codes = min(min_codes, codes)
+    return {"value": n_params / dt / 1e6, "unit": UNIT, "cores": nt, "kind": "port", "seconds": dt,
+            "sample": "layer 0 of the bench workload itself (7 tensors, 25.2 M params, the same weights and "
+                      "262144-token Hessians): EF n_iter 2 (numpy LAPACK factor + C oracle fits and sweeps, "
+                      "all host threads) plus the stock-baseline roundtrip",
+            "parity": {"tensors_checked": checked, "bytes_identical_tensors": same_bytes,
+                       "min_codes_identical": min_codes,
+                       "sample": f"layer 0's 7 tensors whole + the first {rows_big} rows of output.weight and "
+                                 "token_embd.weight, CPU oracle vs the last timed step's device bytes"}}
 
 
 def reference_arm(args, rank, world):
@@ -553,6 +606,12 @@ def gpu_arm(args, rank, world, local_rank):
     total_params, n_tensors = wl.total_params, len(wl.specs)
     merged = gather_stats_to_rank0(dist, st, rank, world)   # every rank's units, per tensor
 
+    # the CPU port on a sample of this workload, checked against the bytes the last timed step
+    # left on the device (before the e2e runs below overwrite the weights with float16 values)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_baseline_on_workload(torch, wl, outputs)
+
     e2e = None
     if not args.no_e2e:
         e2e = measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_sizes, rank, world)
@@ -561,13 +620,13 @@ def gpu_arm(args, rank, world, local_rank):
     if world == 1 and not args.no_gguf:
         gguf_rec = measure_gguf(torch, args, wl)
 
-    cpu = None
+    cpu_ref = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = run_cpu_baseline(args.seed)
         try:
-            cpu.update(run_reference_as_is(args.seed))
+            cpu_ref = run_reference_as_is(args.seed)
         except (RuntimeError, subprocess.TimeoutExpired, ValueError) as e:
-            cpu["reference_as_is"] = {"unavailable": str(e)[:200]}
+            cpu_ref = {"reference_as_is": {"unavailable": str(e)[:200]}}
+        cpu.update(cpu_ref)
 
     big = None
     if not args.no_config4:
@@ -577,6 +636,10 @@ def gpu_arm(args, rank, world, local_rank):
         torch.cuda.empty_cache()
         big = measure_streamed(torch, dist, args, rank, world, local_rank)
         wl = None
+
+    xtx = None
+    if not args.no_config2:
+        xtx = measure_xtx(torch, dist, args, rank, world, local_rank)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -589,7 +652,7 @@ def gpu_arm(args, rank, world, local_rank):
                     [v["rel_err_vs_stock"] for v in merged.values()])) if merged else None,
                 "stats_tensors": len(merged) if merged else 0,
                 "whole_model_seconds_gguf": gguf_rec,
-                "config4": big}
+                "config4": big, "config2": xtx}
         print(json.dumps(line), flush=True)
     return 0
 
@@ -757,6 +820,10 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
     roof = roofline_record(prof, wl.algorithmic(), args.config4_steps, clk)
     peak_gb = torch.cuda.max_memory_allocated() / 1e9
     merged = gather_stats_to_rank0(dist, st, rank, world)
+    e2e = None
+    if not args.no_e2e:
+        e2e = streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, all_sizes, rank, world,
+                           guard, enc)
     rec = None
     if rank == 0:
         rec = {"workload": f"{args.config4_model}-shaped whole-model EF encode, {args.config4_mixture} "
@@ -771,11 +838,236 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
                "gpu_launches": int(launches), "roofline": roof, "clocks": clk,
                "peak_device_gb_rank0": round(peak_gb, 1), "setup_seconds": round(setup_s, 1),
                "stats_median_rel_err_vs_stock": float(np.median([v["rel_err_vs_stock"] for v in merged.values()]))
-               if merged else None, "stats_tensors": len(merged) if merged else 0}
+               if merged else None, "stats_tensors": len(merged) if merged else 0, "e2e": e2e}
     del enc, outputs, flat, jobs, wl
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return rec
+
+
+def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, all_sizes, rank, world, guard, enc):
+    """config[4] end to end through host buffers: every step uploads each batch's float16
+    weights and its Hessians in storage form (float16 bits / hscale + float32 diagonal, which
+    is also the imatrix) from pinned host memory on a copy stream, widens and decodes them on
+    the device, encodes the batch (Encoder.run_stream: the next batch's uploads and factor
+    chains overlap the current batch's sweeps) and copies each finished batch's packed bytes
+    back to pinned host memory; at N > 1 rank 0 gathers the other ranks' bytes over NCCL and
+    copies them out too.  Wall time per step (host clock around synchronised steps), max over
+    ranks."""
+    from perm_b200 import _native as nat
+    from perm_b200.encoder import Job, StreamBatch
+    from perm_b200.shard import gather_to_rank0
+    host_w = {}
+    for b in job_batches:
+        for j in b:
+            h = torch.empty(tuple(j.x.shape), dtype=torch.float16, pin_memory=True)
+            h.copy_(j.x.to(torch.float16))
+            host_w[j.name] = h
+    keys = sorted({j.hkey for b in job_batches for j in b if j.hkey is not None})
+    host_h, d_off, dn = {}, {}, 0
+    for k in keys:
+        sh = wl.stored[k]
+        h = torch.empty(tuple(sh.h16.shape), dtype=torch.float16, pin_memory=True)
+        h.copy_(sh.h16)
+        host_h[k] = (h, float(sh.hscale), sh.d)
+        d_off[k] = dn
+        dn += sh.d
+    host_d32 = torch.empty(max(1, dn), dtype=torch.float32, pin_memory=True)
+    for k in keys:
+        host_d32[d_off[k]:d_off[k] + wl.stored[k].d].copy_(wl.stored[k].diag32)
+    dev_d32 = torch.empty_like(host_d32, device="cuda")
+    host_out = torch.empty(max(1, sum(all_sizes) if rank == 0 else my_bytes), dtype=torch.uint8, pin_memory=True)
+    h2d = sum(h.numel() * 2 for h in host_w.values()) + sum(v[0].numel() * 2 for v in host_h.values()) + dn * 4
+    d2h = sum(all_sizes) if rank == 0 else 0
+    copy_s, work_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream(priority=-1), torch.cuda.Stream()
+    main = torch.cuda.current_stream()
+    base = flat.data_ptr()
+
+    def gen():
+        with torch.cuda.stream(copy_s):   # every diagonal first: the imatrix of every fit
+            dev_d32.copy_(host_d32, non_blocking=True)
+        got_d32 = torch.cuda.Event()
+        got_d32.record(copy_s)
+        work_s.wait_event(got_d32)
+        main.wait_event(got_d32)
+        for jobs in job_batches:
+            hs, diags, ready = {}, {}, {}
+            for k in sorted({j.hkey for j in jobs if j.mode == "EF"}, key=lambda k: -host_h[k][2]):
+                h, hscale, d = host_h[k]
+                with torch.cuda.stream(copy_s):
+                    h16 = torch.empty((d, d), dtype=torch.float16, device="cuda")
+                    h16.copy_(h, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_s)
+                work_s.wait_event(ev)
+                with torch.cuda.stream(work_s):
+                    H = torch.empty((d, d), dtype=torch.float64, device="cuda")
+                nat.check(nat.lib().cp_hessian_decode(nat.ptr(h16), dev_d32.data_ptr() + 4 * d_off[k], hscale, d,
+                                                      nat.ptr(H), nat.stream_ptr(torch, work_s)), "hessian_decode")
+                h16.record_stream(work_s)
+                done = torch.cuda.Event()
+                done.record(work_s)
+                ready[d] = done
+                hs[k] = H
+                diags[k] = wl.stored[k].diag_host
+            staged, new_jobs = [], []
+            for j in jobs:
+                with torch.cuda.stream(copy_s):
+                    x16 = torch.empty(tuple(j.x.shape), dtype=torch.float16, device="cuda")
+                    x16.copy_(host_w[j.name], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_s)
+                work_s.wait_event(ev)
+                with torch.cuda.stream(work_s):
+                    x = x16.float()
+                x16.record_stream(work_s)
+                x.record_stream(main)
+                done = torch.cuda.Event()
+                done.record(work_s)
+                staged.append((done, [j.name]))
+                hk = j.hkey
+                qw = dev_d32[d_off[hk]:d_off[hk] + host_h[hk][2]] if hk is not None else None
+                if j.mode == "EF":
+                    new_jobs.append(Job(j.name, j.ttype, j.mode, x, qw, hk))
+                else:   # token_embd: the attn0 diagonal as fit weights, unit statistics weights
+                    new_jobs.append(Job(j.name, j.ttype, j.mode, x, None, None, fit_w=qw))
+            yield StreamBatch(new_jobs, hs, diags, {j.name: outputs[j.name] for j in jobs}, staged, ready)
+
+    def on_batch(b, raws, st):
+        with torch.cuda.stream(d2h_s):
+            for j in b.jobs:
+                o = outputs[j.name]
+                a = o.data_ptr() - base
+                host_out[a:a + o.numel()].copy_(o.view(-1), non_blocking=True)
+
+    def step():
+        with guard.step():
+            enc.run_stream(gen(), stats=True, on_batch=on_batch if world == 1 else None)
+            if world > 1:
+                bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+                if rank == 0:
+                    off = 0
+                    with torch.cuda.stream(d2h_s):
+                        d2h_s.wait_stream(main)
+                        for bb in bufs:
+                            host_out[off:off + bb.numel()].copy_(bb[:bb.numel()], non_blocking=True)
+                            off += bb.numel()
+            torch.cuda.synchronize()
+
+    step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.config4_steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.config4_steps
+    if world > 1:
+        t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    return {"value": wl.total_params / dt / 1e6, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "seconds_per_step": dt, "steps": args.config4_steps, "warmup": 1,
+            "path": "host float16 weights + storage-form Hessians -> per-batch uploads, device decode -> "
+                    "streamed encode -> host bytes"}
+
+
+def measure_xtx(torch, dist, args, rank, world, local_rank):
+    """Hessian accumulation (the hook arithmetic of hessians.py:137-152,
+    H = x^T x in float32) for the hooked Linear inputs of 28 Qwen3-0.6B-shaped layers, four
+    distinct inputs per layer (q/k/v share d = 1024, attn_output d = 2048, gate/up share
+    d = 1024, ffn_down d = 3072), 262144 bf16 tokens each (N(0, 1) x per-channel log-normal
+    scales), through cp_xtx_accumulate on the tensor cores.  The 112 (layer, input) units are
+    spread over the ranks by cost (d^2, greedy), and at N > 1 rank 0 gathers every rank's
+    float32 [d, d] results over NCCL inside the step.  One bf16 activation matrix per distinct
+    d stays resident (0.5 - 1.6 GB each, larger than L2), so each unit re-reads it from HBM."""
+    from perm_b200 import _native as nat
+    from perm_b200 import hessians
+    from perm_b200.shard import gather_to_rank0
+    T = args.hessian_tokens
+    units = [(layer, kind, d) for layer in range(28)
+             for kind, d in (("qkv", 1024), ("o", 2048), ("gateup", 1024), ("down", 3072))]
+    loads, mine = [0.0] * world, [[] for _ in range(world)]
+    for u in sorted(units, key=lambda u: -u[2]):
+        r = min(range(world), key=lambda i: loads[i])
+        loads[r] += float(u[2]) ** 2
+        mine[r].append(u)
+    my = mine[rank]
+    sizes = [sum(d * d * 4 for _, _, d in mine[r]) for r in range(world)]
+    flat = torch.empty(max(1, sizes[rank] // 4), dtype=torch.float32, device="cuda")
+    Hs, off = [], 0
+    for _, _, d in my:
+        Hs.append(flat[off:off + d * d].view(d, d))
+        off += d * d
+    X = {}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(args.seed * 31 + 7)
+    for d in sorted({u[2] for u in units}):
+        scales = torch.exp(torch.randn(d, generator=g, device="cuda"))
+        X[d] = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
+        for t0 in range(0, T, 32768):
+            X[d][t0:t0 + 32768] = (torch.randn((min(32768, T - t0), d), generator=g, device="cuda") *
+                                   scales).to(torch.bfloat16)
+    flops = sum(2.0 * T * d * d for _, _, d in units)
+    guard = make_guard(dist, rank, world)
+
+    def step():
+        with guard.step():
+            flat.zero_()
+            for (_, _, d), H in zip(my, Hs):
+                hessians.xtx_accumulate(X[d], H)
+            if world > 1:
+                gather_to_rank0(torch, dist, flat.view(torch.uint8)[:sizes[rank]], sizes, rank, world)
+
+    if world > 1:
+        dist.barrier()
+    for _ in range(args.warmup):
+        step()
+    hessians.xtx_status()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    nat.profile_enable(True)
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        step()
+    t_end.record()
+    torch.cuda.synchronize()
+    nat.profile_enable(False)
+    prof = nat.profile_collect()
+    hessians.xtx_status()
+    if world > 1:
+        dist.barrier()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kms = prof["other"][0] / args.steps   # the X^T X launches (this rank)
+    my_flops = sum(2.0 * T * d * d for _, _, d in my)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    del X, flat, Hs
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    ach = my_flops / (kms / 1e3) / 1e12 if kms > 0 else None
+    return {"workload": "28 Qwen3-0.6B-shaped layers x 4 distinct Linear inputs (d 1024, 2048, 1024, 3072), "
+                        f"{T} bf16 tokens each: H = x^T x in float32",
+            "ms_per_step": ms, "seconds_per_step": ms / 1e3, "tflops_whole_job": flops / (ms / 1e3) / 1e12,
+            "tokens_per_s_per_input": 112 * T / (ms / 1e3), "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "units_rank0": len(my),
+            "parallelism": "(layer, input) units by cost over the ranks, NCCL gather of the float32 [d, d] "
+                           "results to rank 0 inside the step" if world > 1 else "one GPU",
+            "roofline": {"kernel": "xtx_tc_kernel (tcgen05 kind::f16, TMEM accumulators)", "bound": "tensor",
+                         "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak if ach else None,
+                         "work": "2 T d^2 per (layer, input) unit (algorithmic, lower triangle computed once)",
+                         "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if "bf16_tflops" in peaks
+                         else "fallback 1590 TFLOP/s", "ms_per_step": kms}}
 
 
 def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_sizes, rank, world):
