@@ -1,6 +1,6 @@
 """Small, fixed micro-cases of the encoder's kernels, for timing and for profiler captures
 (`ncu ... python bench_cases.py <case>`).  Each case holds at most a few hundred MB
-on the device and runs its kernels a few times.
+on the device (llama_layers: about 30 GB) and runs its kernels a few times.
 
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
     sweep_layers  eight Qwen3-0.6B-shaped layers (56 tensors), grouped EF sweep
@@ -8,6 +8,8 @@ on the device and runs its kernels a few times.
     fit      Q2_K imatrix fit of a 4096 x 4096 tensor
     factor   batched FP64 factorisation of 16 Hessians n = 1024 and 4 of n = 3072
     factor_model  the whole 0.6B model's 112 factorisations
+    factor_rank8  one rank's share of an 8-GPU plan's factorisations (latency-bound)
+    llama_layers  four Llama-3-8B-shaped layers streamed in two batches (config[4] pipeline)
     xtx      X^T X of 32768 bf16 tokens at d = 1024, 2048, 3072 (tcgen05 kernel)
     xtx_f32  the same with float32 tokens (hi/lo bf16 split, four products)
 """
@@ -175,6 +177,40 @@ def case_factor_rank8(torch, reps):
     return f"factor_rank8 3x3072 + 4x2048 + 7x1024: {dt * 1e3:.2f} ms, {fl / dt / 1e12:.2f} FP64 TFLOP/s"
 
 
+def case_llama_layers(torch, reps):
+    """Four Llama-3-8B-shaped layers (q/k/v/o, gate/up 14336 x 4096, down 4096 x 14336; the
+    Q4_K_M-style mixture) streamed through Encoder.run_stream in two batches of two layers,
+    Hessians resident in storage form (from 8192 synthetic tokens) and decoded per batch: the
+    config[4] pipeline at a size a profiler capture can hold (about 25 GB)."""
+    from perm_b200 import model, stream as stm
+    from perm_b200.encoder import Encoder, Job
+    cfg = dict(model.MODELS["llama3-8b"], n_layers=4)
+    specs = [sp for sp in model.tensor_specs(cfg, "q4_k_m_style") if sp.name.startswith("blk.")]
+    dims = model.hessian_dims(specs)
+    stored = {}
+    for k, d in dims.items():
+        stored[k] = stm.store_hessian(torch, model.synth_hessian(torch, d, k, 0, "cuda", tokens=8192))
+    jobs = []
+    for sp in specs:
+        x = model.synth_weights(torch, sp, 0, "cuda")
+        qw = torch.from_numpy(stored[sp.hkey].diag_host.astype(np.float32)).cuda()
+        jobs.append(Job(sp.name, sp.ttype, "EF", x, qw, sp.hkey))
+    per_layer = sum(j.params for j in jobs) / 4
+    plan = stm.plan(jobs, dims, 2 * per_layer * stm.ef_bytes_per_param() + 2 * (stm.hessian_bytes(14336) +
+                                                                               3 * stm.hessian_bytes(4096)))
+    enc = Encoder()
+    dec = torch.cuda.Stream(priority=-1)
+    enc.run_stream(stm.batches(torch, plan, stored, None, dec))
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        enc.run_stream(stm.batches(torch, plan, stored, None, dec))
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t) / reps
+    params = sum(j.params for j in jobs)
+    return f"llama_layers 4 layers, {len(plan)} batches: {dt * 1e3:.1f} ms, {params / dt / 1e6:.0f} Mparams/s"
+
+
 def case_xtx(torch, reps, dtype="bf16"):
     from perm_b200 import hessians
     out = []
@@ -205,13 +241,17 @@ def case_xtx_f32(torch, reps):
     return case_xtx(torch, reps, "f32")
 
 
-CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "factor_rank8": case_factor_rank8, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
+CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "factor_rank8": case_factor_rank8, "llama_layers": case_llama_layers, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):
     import torch
-    names = argv or list(CASES)
     reps = 3
+    if "--reps" in argv:
+        i = argv.index("--reps")
+        reps = int(argv[i + 1])
+        argv = argv[:i] + argv[i + 2:]
+    names = argv or list(CASES)
     for n in names:
         print(CASES[n](torch, reps), flush=True)
 
