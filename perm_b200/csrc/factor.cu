@@ -449,12 +449,11 @@ __global__ void __launch_bounds__(kFT) trsm_panel_kernel(const __grid_constant__
 // Cholesky chain no longer touches it), the diagonal inverses come transposed from D, and the
 // off-diagonal blocks of Linv are kept transposed in the strict upper triangle of P, which
 // the Cholesky chain never reads.  Each result also goes straight to U (reversed, cast).
-// One CTA per (column tile, item); T holds each tile's intermediate product.
-__global__ void __launch_bounds__(kFT) trinv_row_kernel(const __grid_constant__ FactorBatch fb, int j) {
-  const int n = fb.n;
-  double* __restrict__ P = fb.P[blockIdx.y];
-  if (*fb.status[blockIdx.y]) return;
-  const int c0 = blockIdx.x * 64;
+// Tile c reduces over j - 64c columns, so a CTA takes tiles c and nt - 1 - c together: every
+// CTA then does the same work (j + 192 columns of products) and a launch has no long tail.
+// T holds each tile's intermediate product.
+__device__ __forceinline__ void trinv_row_tile(const FactorBatch& fb, double* __restrict__ P, int n, int j, int c0,
+                                               int item) {
   double* __restrict__ S = t_base(P, n) + (size_t)c0 * 64;   // S[c][r] = product[r][c]
   double acc[2][4][4];
   tile64<true>(P + (size_t)j * n + c0, n, d_base(P, n) + (size_t)c0 * 64, 64, 64, 64, 64, acc, false);
@@ -467,9 +466,21 @@ __global__ void __launch_bounds__(kFT) trinv_row_kernel(const __grid_constant__ 
   tile_for_each(acc, [&](int r, int c, double v) {
     P[(size_t)(c0 + c) * n + j + r] = -v;
     const size_t u = (size_t)(n - 1 - (j + r)) * n + (size_t)(n - 1 - (c0 + c));
-    if (fb.out_f64) static_cast<double*>(fb.U[blockIdx.y])[u] = -v;
-    else static_cast<float*>(fb.U[blockIdx.y])[u] = (float)(-v);
+    if (fb.out_f64) static_cast<double*>(fb.U[item])[u] = -v;
+    else static_cast<float*>(fb.U[item])[u] = (float)(-v);
   });
+}
+
+__global__ void __launch_bounds__(kFT) trinv_row_kernel(const __grid_constant__ FactorBatch fb, int j) {
+  const int n = fb.n, item = blockIdx.y;
+  double* __restrict__ P = fb.P[item];
+  if (*fb.status[item]) return;
+  const int nt = j / 64, ca = blockIdx.x, cb = nt - 1 - blockIdx.x;
+  trinv_row_tile(fb, P, n, j, ca * 64, item);
+  if (cb > ca) {
+    __syncthreads();   // the first tile's last shared-memory reads are done
+    trinv_row_tile(fb, P, n, j, cb * 64, item);
+  }
 }
 
 size_t factor_workspace_bytes(int64_t n) {
@@ -553,7 +564,7 @@ int launch_factor_batch(const FactorBatch& fb, cudaStream_t stream) {
     if (j > 0) {   // block row j of the inverse, on the helper stream
       cudaEventRecord(hp->step, stream);
       cudaStreamWaitEvent(hp->s, hp->step, 0);
-      trinv_row_kernel<<<dim3((unsigned)(j / 64), (unsigned)cnt), kFT, 0, hp->s>>>(fb, j);
+      trinv_row_kernel<<<dim3((unsigned)((j / 64 + 1) / 2), (unsigned)cnt), kFT, 0, hp->s>>>(fb, j);
       note_launch();
     }
     if (n - j - NB > 0) {
