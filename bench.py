@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--config4-steps", type=int, default=2)
     ap.add_argument("--config4-warmup", type=int, default=3)
     ap.add_argument("--config4-budget-gb", type=float, default=0.0,
-                    help="device bytes per batch (0: 40%% of the memory free once the inputs are resident)")
+                    help="device bytes per batch (0: 30%% of the memory free once the inputs are resident)")
     return ap.parse_args()
 
 
@@ -774,7 +774,7 @@ def measure_streamed(torch, dist, args, rank, world, local_rank):
         all_sizes = [my_bytes]
     torch.cuda.synchronize()
     free, _total = torch.cuda.mem_get_info()
-    budget = args.config4_budget_gb * 1e9 if args.config4_budget_gb > 0 else 0.40 * free
+    budget = args.config4_budget_gb * 1e9 if args.config4_budget_gb > 0 else 0.30 * free
     job_batches = stm.plan(jobs, wl.dims, budget)
     enc = Encoder(n_iter=2, damp=0.01, act_order=True)
     dec = torch.cuda.Stream(priority=-1)
