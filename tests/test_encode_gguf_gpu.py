@@ -80,3 +80,61 @@ def test_encode_gguf_batches_and_timings(tmp_path, orc):
         assert set(st1[k]) == {"type", "mode", "rel_err_vs_stock", "sec"}
     assert tm["batches"] >= 4 and tm["tensors"] == len(fx.SPEC)
     assert tm["h2d_bytes"] > 0 and tm["d2h_bytes"] > 0 and tm["wall_s"] >= tm["write_s"]
+
+
+class _PermSpacemap:
+    """Stand-in for a PERM spacemap (perm/spacemaps): input_perm(name, perms, dims) returns the
+    input permutation of a tensor, or None for tensors it does not permute."""
+
+    def __init__(self, table):
+        self.table = table
+
+    def input_perm(self, name, perms, dims, **_):
+        return self.table.get(name)
+
+
+def test_encode_gguf_with_input_permutations(tmp_path, orc):
+    """ef.py:289-290 and 272-276: with PERM permutations the imatrix and the Hessian are
+    permuted (qw[p], H[p][:, p]) while the weights are read as stored; token_embd's fit
+    weights are permuted too.  Every output must match the oracle run on the permuted inputs,
+    and identical Hessians under different permutations must not be shared."""
+    from gguf import GGUFReader
+    from perm_b200 import ef, gguf_io
+    W = fx.weights()
+    f16, tgt, out = str(tmp_path / "f16.gguf"), str(tmp_path / "t.gguf"), str(tmp_path / "o.gguf")
+    hdir, imp = str(tmp_path / "hess"), str(tmp_path / "im.gguf")
+    fx.write_f16(f16, W)
+    fx.write_target(tgt, W, orc.quantize)
+    gguf_io.save_hessians(fx.hessians(), hdir)
+    fx.write_imatrix(imp, [(n, ne0) for n, tt, ne0, nrow in fx.SPEC if n != "token_embd.weight"])
+    rng = np.random.default_rng(17)
+    ne0 = {n: e for n, tt, e, nrow in fx.SPEC}
+    table = {n: rng.permutation(ne0[n]) for n in ("token_embd.weight", "blk.0.attn_q.weight",
+                                                  "blk.0.ffn_down.weight", "blk.0.ffn_up.weight")}
+    stats = ef.encode_gguf(f16, tgt, hdir, out, imatrix_path=imp, perms={"any": 1}, spacemap=_PermSpacemap(table),
+                           log=lambda *_: None, max_params_per_batch=150_000)
+    imat = gguf_io.imatrix_means(imp)
+    got = {t.name: np.asarray(t.data) for t in GGUFReader(out).tensors}
+    for name, tt, e, nrow in fx.SPEC:
+        x = W[name].astype(np.float16).astype(np.float32)
+        p = table.get(name)
+        qw = imat.get(name)
+        if qw is not None and p is not None:
+            qw = qw[p]
+        if name == "token_embd.weight":
+            H0, n0 = gguf_io.load_hessian(hdir, "blk.0.attn_q.weight")
+            fw = (np.diag(H0) / n0).astype(np.float32)
+            want = orc.quantize(tt, x, fw[p] if p is not None else fw)
+            assert np.array_equal(got[name].reshape(want.shape), want), name
+        elif gguf_io.has_hessian(hdir, name):
+            H, _ = gguf_io.load_hessian(hdir, name)
+            if p is not None:
+                H = H[np.ix_(p, p)]
+            want, _ = orc.ef_encode(x, tt, qw, H, n_iter=2, act_order=True)
+            g = got[name].reshape(want.shape)
+            frac = float(np.mean(orc.codes(tt, g, nrow, e) == orc.codes(tt, want, nrow, e)))
+            assert frac >= 0.999, f"{name}: codes identical {frac:.4%}"
+        else:
+            want = orc.quantize(tt, x, qw)
+            assert np.array_equal(got[name].reshape(want.shape), want), name
+    assert set(stats) == {n for n, *_ in fx.SPEC}
