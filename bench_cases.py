@@ -3,6 +3,7 @@
 on the device (llama_layers: about 30 GB) and runs its kernels a few times.
 
     sweep    24 Q2_K tensors 1024 x 1024 plus 8 Q3_K tensors 1024 x 3072, grouped EF sweep
+    sweep_wide    40 Q2_K tensors 4096 x 1024, the ordinary (unsplit) sweep form
     sweep_layers  eight Qwen3-0.6B-shaped layers (56 tensors), grouped EF sweep
     sweep_model   all 28 layers' EF tensors (196 tensors), the whole-model sweep launch
     fit      Q2_K imatrix fit of a 4096 x 4096 tensor
@@ -61,6 +62,15 @@ def case_sweep(torch, reps):
     shapes = [(1024, 1024, "Q2_K", "h1024")] * 24 + [(1024, 3072, "Q3_K", "h3072")] * 8
     ms, upd = _sweep_case(torch, reps, shapes)
     return f"sweep: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s"
+
+
+def case_sweep_wide(torch, reps):
+    """40 Q2_K tensors 4096 x 1024 over 8 Hessians (1280 CTAs: enough for the ordinary sweep
+    form, which launches of fewer than 8 x 148 CTAs do not use), about 3 GB on the device."""
+    shapes = [(4096, 1024, "Q2_K", f"h{i % 8}") for i in range(40)]
+    ms, upd = _sweep_case(torch, reps, shapes)
+    return (f"sweep_wide: {ms:.3f} ms per 2-round encode, {upd / ms / 1e9:.2f} T ordered updates/s, "
+            f"{2 * upd / ms / 1e9:.2f} T fp32 lane-ops/s")
 
 
 def case_sweep_model(torch, reps):
@@ -241,7 +251,7 @@ def case_xtx_f32(torch, reps):
     return case_xtx(torch, reps, "f32")
 
 
-CASES = {"sweep": case_sweep, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "factor_rank8": case_factor_rank8, "llama_layers": case_llama_layers, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
+CASES = {"sweep": case_sweep, "sweep_wide": case_sweep_wide, "sweep_layers": case_sweep_layers, "sweep_model": case_sweep_model, "fit": case_fit, "factor": case_factor, "factor_model": case_factor_model, "factor_rank8": case_factor_rank8, "llama_layers": case_llama_layers, "xtx": case_xtx, "xtx_f32": case_xtx_f32}
 
 
 def main(argv):
