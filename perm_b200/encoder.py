@@ -14,7 +14,9 @@ and always computes the stock baseline roundtrip(x, type, qw) for the statistics
     and the stats need no extra fit;
   * the weighted squared errors are reduced on the device; one device-to-host copy at the end.
 """
+import contextlib
 import ctypes
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -90,18 +92,33 @@ class Encoder:
     transposes; False keeps everything row-major."""
 
     def __init__(self, n_iter=2, damp=0.01, act_order=True, stream=None, log=None, overlap_sweeps=False,
-                 factor_priority=-1, column_major=True):
+                 factor_priority=-1, column_major=True, nvtx=None):
         self.torch = nat.torch_cuda()
         self.n_iter, self.damp, self.act_order = n_iter, damp, act_order
         self.overlap_sweeps, self.factor_priority = overlap_sweeps, factor_priority
         self.column_major = column_major
         self.stream = stream
         self.log = log
+        # NVTX ranges around every stage's launches (fits, factor chains, grids, sweeps,
+        # transposes and repacks, statistics), for nsys / ncu --nvtx; on when nvtx=True or the
+        # environment sets PERM_B200_NVTX=1
+        self.nvtx = nvtx if nvtx is not None else os.environ.get("PERM_B200_NVTX", "") not in ("", "0")
         self._ws = None
         self._fws = {}            # n -> factor workspaces, reused in stream order
         self._fstreams = {}       # n -> factorisation stream
         self._fstage = {}         # n -> ring of [pinned act-order staging, event of its last read]
         self._fstage_next = {}
+
+    @contextlib.contextmanager
+    def _range(self, name):
+        if not self.nvtx:
+            yield
+            return
+        self.torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            self.torch.cuda.nvtx.range_pop()
 
     # ---------------------------------------------------------------- factorisation
     def _fstream(self, n):
@@ -202,7 +219,8 @@ class Encoder:
                                           wss[r].data_ptr(), status[slot[k]:slot[k] + 1].data_ptr()))
                 out[k] = Factor(U, ohn[r].astype(np.int64), od[r], self.damp, ut2g[r])
             arr = nat.job_array(nat.FactorJob, jobs)
-            nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
+            with self._range(f"factor n={n} x{len(grp)}"):
+                nat.check(L.cp_factor_u_batch(ctypes.cast(arr, ctypes.c_void_p), len(grp), sp), "factor_u_batch")
             for k in grp:
                 nat.check(L.cp_ef_prepare_u(nat.ptr(out[k].U), n, nat.ptr(out[k].ut2), sp), "prepare_u")
             done = torch.cuda.Event()
@@ -430,14 +448,16 @@ class Encoder:
                                                              int(x.shape[0]), int(x.shape[1])))
             for tt, lst in by_type.items():
                 arr = nat.job_array(nat.FitJob, lst)
-                nat.check(L.cp_kquant_encode_batch(TYPE_ID[tt], ctypes.cast(arr, ctypes.c_void_p), len(lst), s),
-                          "kquant_encode_batch")
+                with self._range(f"fit {tt} x{len(lst)}"):
+                    nat.check(L.cp_kquant_encode_batch(TYPE_ID[tt], ctypes.cast(arr, ctypes.c_void_p), len(lst), s),
+                              "kquant_encode_batch")
 
         def block_call(fn, items, what):
             if not items:
                 return
             arr = nat.job_array(nat.BlockJob, items)
-            nat.check(fn(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
+            with self._range(what):
+                nat.check(fn(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
 
         cm = self.column_major
         pitch = {i: int(L.cp_ef_sweep_rows(int(jobs[i].x.shape[0]))) for i in ef_idx} if cm else {}
@@ -446,7 +466,8 @@ class Encoder:
             if not items:
                 return
             arr = nat.job_array(nat.TransposeJob, [nat.TransposeJob(*it) for it in items])
-            nat.check(L.cp_transpose_batch(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
+            with self._range(what):
+                nat.check(L.cp_transpose_batch(ctypes.cast(arr, ctypes.c_void_p), len(items), s), what)
 
         def werr_items(idx_list, col, use_base=False):
             out = []
@@ -542,7 +563,9 @@ class Encoder:
                                            nat.addr(views[i]["work"]), pitch.get(i, 0)))
                 if sw:
                     arr = nat.job_array(nat.SweepJob, sw)
-                    nat.check(L.cp_ef_sweep_batch(ctypes.cast(arr, ctypes.c_void_p), len(sw), s), "ef_sweep_batch")
+                    with self._range(f"sweep round {it + 1} x{len(sw)}"):
+                        nat.check(L.cp_ef_sweep_batch(ctypes.cast(arr, ctypes.c_void_p), len(sw), s),
+                                  "ef_sweep_batch")
             if it == 0 and factor_event:
                 for n in factor_event:   # everything after this point needs every factor
                     main.wait_event(factor_event[n])

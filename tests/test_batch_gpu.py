@@ -181,3 +181,20 @@ def test_medium_launch_matches_oracle(orc):
     for name, tt, mode, W, qw, hk, fw in jobs:
         want, _ = orc.ef_encode(W, tt, qw, hess[hk], n_iter=2, act_order=True)
         assert np.array_equal(got[name], want), f"{name} {tt}: {np.count_nonzero(got[name] != want)} bytes differ"
+
+
+def test_nvtx_ranges_change_nothing():
+    """Encoder(nvtx=True) wraps every stage's launches in NVTX ranges (for nsys / ncu --nvtx):
+    the bytes and statistics are those of the unannotated run."""
+    import torch
+    from perm_b200.encoder import Encoder, Job
+    rng = np.random.default_rng(12)
+    H = _hessian(rng, 512)
+    hd = {"h": torch.from_numpy(H).cuda()}
+    W = (rng.standard_normal((200, 512)) * 0.02).astype(np.float32)
+    jobs = [Job("t", "Q4_K", "EF", torch.from_numpy(W).cuda(), torch.from_numpy(np.diag(H).astype(np.float32)).cuda(),
+                "h")]
+    a, sa = Encoder(nvtx=False).run(jobs, hd, {"h": np.diag(H)})
+    b, sb = Encoder(nvtx=True).run(jobs, hd, {"h": np.diag(H)})
+    assert np.array_equal(a["t"].cpu().numpy(), b["t"].cpu().numpy())
+    assert sa["t"]["rel_err_vs_stock"] == pytest.approx(sb["t"]["rel_err_vs_stock"], rel=1e-9)
