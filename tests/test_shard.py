@@ -5,16 +5,17 @@ import numpy as np
 import pytest
 
 
-def _metas():
+def _metas(model_name="qwen3-0.6b", mixture="q2_k_mix"):
     from perm_b200 import model, shard
-    specs = model.tensor_specs(model.MODELS["qwen3-0.6b"], "q2_k_mix")
+    specs = model.tensor_specs(model.MODELS[model_name], mixture)
     return specs, [shard.UnitMeta(s.name, s.ttype, s.mode, s.nrow, s.n, s.hkey, True) for s in specs]
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_plan_covers_every_row_once_and_balances(world):
+@pytest.mark.parametrize("model_name,mixture", [("qwen3-0.6b", "q2_k_mix"), ("llama3-8b", "q4_k_m_style")])
+def test_plan_covers_every_row_once_and_balances(world, model_name, mixture):
     from perm_b200 import shard
-    specs, metas = _metas()
+    specs, metas = _metas(model_name, mixture)
     plan = shard.make_plan(metas, world)
     rows = {s.name: np.zeros(s.nrow, np.int32) for s in specs}
     for r in range(world):
