@@ -328,6 +328,11 @@ class Encoder:
             r2, s2 = self.encode(again, d.factors, stats=d.stats, outputs={j.name: d.raws[j.name] for j in again},
                                  after_pack=d.after_pack)
             st.update(s2)
+            # the re-encoded bytes are final only once the stream reaches them; callers copy
+            # the bytes out on other streams as soon as finish() returns
+            done = self.torch.cuda.Event()
+            done.record(self.stream if self.stream is not None else self.torch.cuda.current_stream())
+            done.synchronize()
         return d.raws, st
 
     def run_stream(self, batches, stats=True, on_batch=None):
