@@ -1054,9 +1054,9 @@ def measure_xtx(torch, dist, args, rank, world, local_rank):
     kms = prof["other"][0] / args.steps   # the X^T X launches (this rank)
     my_flops = sum(2.0 * T * d * d for _, _, d in my)
 
-    def executed(d):   # tensor-core flops of one unit: 128 x 256 tiles on or below the diagonal
-        nt = -(-d // 128)
-        return 2.0 * T * 128 * 256 * sum(ti // 2 + 1 for ti in range(nt))
+    def executed(d):   # tensor-core flops of one unit: 256 x 256 pair tiles on or below the diagonal
+        nT = -(-d // 256)
+        return 2.0 * T * 256 * 256 * (nT * (nT + 1) // 2)
     my_exec = sum(executed(d) for _, _, d in my)
     peaks = {}
     try:
@@ -1077,9 +1077,10 @@ def measure_xtx(torch, dist, args, rank, world, local_rank):
             "n_gpus": world, "units_rank0": len(my),
             "parallelism": "(layer, input) units by cost over the ranks, NCCL gather of the float32 [d, d] "
                            "results to rank 0 inside the step" if world > 1 else "one GPU",
-            "roofline": {"kernel": "xtx_tc_kernel (tcgen05 kind::f16, TMEM accumulators)", "bound": "tensor",
+            "roofline": {"kernel": "xtx_pair_kernel (tcgen05.mma.cta_group::2 kind::f16, TMEM accumulators)",
+                         "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak if ach else None,
-                         "work": "tensor-core flops executed: 2 T x 128 x 256 per tile on or below the diagonal "
+                         "work": "tensor-core flops executed: 2 T x 256 x 256 per pair tile on or below the diagonal "
                                  "(H is symmetric, so about 55 % of a dense 2 T d^2)",
                          "algorithmic_equivalent_tflops": ach_alg,
                          "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if "bf16_tflops" in peaks

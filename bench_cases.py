@@ -135,10 +135,9 @@ def case_factor(torch, reps):
 
 
 def _xtx_tile_flops(T, d):
-    """Flops the tensor cores execute: 128 x 256 tiles on or below the diagonal."""
-    nt = -(-d // 128)
-    tiles = sum(ti // 2 + 1 for ti in range(nt))
-    return 2.0 * tiles * 128 * 256 * T
+    """Flops the tensor cores execute: 256 x 256 pair tiles on or below the diagonal."""
+    nT = -(-d // 256)
+    return 2.0 * (nT * (nT + 1) // 2) * 256 * 256 * T
 
 
 def case_factor_model(torch, reps):

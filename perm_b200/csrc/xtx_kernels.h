@@ -9,11 +9,16 @@ namespace cpk {
 // Launch shape and workspace layout of one X^T X call (all offsets in bytes).
 struct XtxPlan {
   int nt;               // 128-wide blocks of d
-  int tiles;            // 128 x 256 tiles on or below the diagonal
+  int pairs;            // 256 x 256 tiles on or below the diagonal (one CTA pair each)
   int phases;           // 1 (bf16 input) or 4 (float32 input split into hi/lo bf16)
   int ki;               // 64-token steps per phase
+  int total;            // 64-token steps per pair tile (phases * ki)
   int splits;           // token splits
-  int steps_per_split;
+  int per;              // 64-token steps per split
+  int full_items;       // regular (split, pair) items run in whole rounds
+  int rem_q, sub_per;   // the remaining regular items are cut into rem_q sub-items of sub_per steps
+  int items;            // full_items + remaining regular items * rem_q
+  int clusters;         // CTA pairs of the persistent launch
   size_t off_partial, off_hi, off_lo, ws_bytes;
 };
 

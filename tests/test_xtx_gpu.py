@@ -1,5 +1,5 @@
 """cp_xtx_accumulate (the tensor-core X^T X of Hessian collection, coldpress/hessians.py:
-455-470) against a float64 product of the same activations, through the C ABI.
+137-152) against a float64 product of the same activations, through the C ABI.
 
 Tolerance.  The reference forms x.T @ x in float32 (`x.float()` first), so its own result
 carries float32 matmul rounding.  Errors here are measured element-wise against the float64
@@ -8,7 +8,10 @@ tensor-core result must stay within 4x the error of torch's float32 matmul on th
 activations (floor 2^-22).  bf16 activations give exact float32 products; float32
 activations are split into hi + lo bf16 (2^-17 relative remainder) and must also beat a
 plain bf16 cast of the activations by 20x.  H must stay exactly symmetric and two runs must
-give identical bits (split-K partials are summed in a fixed order).
+give identical bits (the per-item partial tiles are summed in token order).  The shapes cover
+the kernel's schedules: one pair tile cut over the SM pairs (d <= 256), whole rounds of pair
+tiles plus a last round of sub-items (d = 3072, 4096), and several token splits per pair tile
+(262144 x 1024).
 """
 import numpy as np
 import pytest
@@ -57,7 +60,7 @@ def torch_sqrt_diag(xtx):
 
 
 @pytest.mark.parametrize("T,d", [(1, 128), (37, 8), (100, 136), (4096, 1024), (20000, 520), (3000, 3072),
-                                 (777, 2048), (16384, 4096), (262144, 256)])
+                                 (777, 2048), (16384, 4096), (262144, 256), (262144, 1024)])
 def test_xtx_bf16_matches_float64(T, d):
     torch, nat, L = _lib()
     x = _acts(torch, T, d, T * 31 + d, torch.bfloat16)
