@@ -246,8 +246,9 @@ int cp_factor_u_batch(const cp_factor_job* jobs, int count, void* stream);
 #define CP_XTX_F32 1
 
 /* Device workspace that cp_xtx_accumulate needs for x of `dtype` [T, d] on the current
- * device: a status word, per-tile counters, token-split partial tiles and, for float32
- * input, the hi/lo bf16 copies of x.  Zero-fill it once when it is allocated. */
+ * device: a status word, one partial tile per work item (a 256 x 256 tile over a token
+ * range) and, for float32 input, the hi/lo bf16 copies of x.  Zero-fill it once when it is
+ * allocated. */
 size_t cp_xtx_workspace_bytes(int dtype, int64_t T, int64_t d);
 
 /* hessians.py:137-152 hook arithmetic (`x.float(); acc += x.T @ x`): H += x^T x for x
@@ -260,7 +261,7 @@ int cp_xtx_accumulate(int dtype, const void* x, int64_t T, int64_t d, float* H, 
 
 /* Failure-path testing of the bounded waits (no counterpart in the reference): arms the
  * calling thread's NEXT cp_xtx_accumulate so that its loader issues no loads for the 64-token
- * step `skip_step` and every wait in that call gives up after wait_ns nanoseconds
+ * step `skip_step` (of every tile) and every wait in that call gives up after wait_ns nanoseconds
  * (1 us .. 2 s).  The waits on the unfilled stage then run out, the kernel stops, drains the
  * loads it did issue, frees its tensor memory and sets the status word, so cp_xtx_status
  * returns CP_ERR_TIMEOUT and the device stays usable.  Nothing else changes; one call only. */
