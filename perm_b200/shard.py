@@ -22,8 +22,12 @@ from dataclasses import dataclass, field
 FIT_PASSES = {("Q2_K", True): 38, ("Q2_K", False): 17, ("Q3_K", True): 19, ("Q3_K", False): 6,
               ("Q4_K", True): 38, ("Q4_K", False): 22, ("Q5_K", True): 38, ("Q5_K", False): 17,
               ("Q6_K", True): 19, ("Q6_K", False): 19}
-FIT_OP_WEIGHT = 10.0      # ops per candidate-element relative to one ordered update
-FACTOR_WEIGHT = 4.0       # FP64 flop relative to one ordered update
+# Relative weights, fitted to B200 times of every rank's share of the 4- and 8-way plans of
+# the 0.6B model (one GPU per share, least squares over sweep updates, candidate evaluations
+# and FP64 flops; residuals under 0.5 ms): one candidate-element evaluation of a fit costs
+# about 20 ordered updates, one FP64 flop of the factorisation about one.
+FIT_OP_WEIGHT = 20.0      # candidate-element evaluation relative to one ordered update
+FACTOR_WEIGHT = 1.0       # FP64 flop relative to one ordered update
 
 
 @dataclass
