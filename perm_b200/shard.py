@@ -28,6 +28,7 @@ FIT_PASSES = {("Q2_K", True): 38, ("Q2_K", False): 17, ("Q3_K", True): 19, ("Q3_
 # about 20 ordered updates, one FP64 flop of the factorisation about one.
 FIT_OP_WEIGHT = 20.0      # candidate-element evaluation relative to one ordered update
 FACTOR_WEIGHT = 1.0       # FP64 flop relative to one ordered update
+WRTN_FITS = 2.0           # fit passes charged to a weighted-RTN tensor (its fit and the stock baseline)
 
 
 @dataclass
@@ -64,7 +65,7 @@ def unit_cost(m, rows, n_iter=2):
     if m.mode == "EF":
         return n_iter * (rows * m.n * (m.n - 1) / 2.0) + n_iter * fit
     if m.mode == "wRTN(attn0-diag)":
-        return 2 * fit
+        return WRTN_FITS * fit
     return fit
 
 
