@@ -861,7 +861,7 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
     ranks."""
     from perm_b200 import _native as nat
     from perm_b200.encoder import Job, StreamBatch
-    from perm_b200.shard import gather_to_rank0
+    from perm_b200.shard import HostGather, gather_to_rank0
     host_w = {}
     for b in job_batches:
         for j in b:
@@ -884,7 +884,16 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
     for k in keys:
         host_d32[d_off[k]:d_off[k] + wl.stored[k].d].copy_(wl.stored[k].diag32)
     dev_d32 = torch.empty_like(host_d32, device="cuda")
-    host_out = torch.empty(max(1, sum(all_sizes) if rank == 0 else my_bytes), dtype=torch.uint8, pin_memory=True)
+    # N > 1: each batch's bytes go over the rank's own link into one shared host buffer that rank
+    # 0 reads (HostGather); without room in /dev/shm, the NCCL gather and rank 0's copy instead
+    hg, hg_note = None, None
+    if world > 1:
+        try:
+            hg = HostGather(torch, dist, all_sizes, rank, world)
+        except OSError as e:
+            hg_note = str(e)
+    host_out = torch.empty(max(1, my_bytes if world == 1 else (sum(all_sizes) if rank == 0 and hg is None else 0)),
+                           dtype=torch.uint8, pin_memory=True)
     h2d = sum(h.numel() * 2 for h in host_w.values()) + sum(v[0].numel() * 2 for v in host_h.values()) + dn * 4
     d2h = sum(all_sizes) if rank == 0 else 0
     copy_s, work_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream(priority=-1), torch.cuda.Stream()
@@ -942,16 +951,17 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
             yield StreamBatch(new_jobs, hs, diags, {j.name: outputs[j.name] for j in jobs}, staged, ready)
 
     def on_batch(b, raws, st):
+        dst = hg.mine if hg is not None else host_out
         with torch.cuda.stream(d2h_s):
             for j in b.jobs:
                 o = outputs[j.name]
                 a = o.data_ptr() - base
-                host_out[a:a + o.numel()].copy_(o.view(-1), non_blocking=True)
+                dst[a:a + o.numel()].copy_(o.view(-1), non_blocking=True)
 
     def step():
         with guard.step():
-            enc.run_stream(gen(), stats=True, on_batch=on_batch if world == 1 else None)
-            if world > 1:
+            enc.run_stream(gen(), stats=True, on_batch=on_batch if (world == 1 or hg is not None) else None)
+            if world > 1 and hg is None:
                 bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
                 if rank == 0:
                     off = 0
@@ -961,6 +971,8 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
                             host_out[off:off + bb.numel()].copy_(bb[:bb.numel()], non_blocking=True)
                             off += bb.numel()
             torch.cuda.synchronize()
+            if hg is not None:
+                hg.barrier()   # every rank's bytes are in rank 0's host buffer
 
     step()
     if world > 1:
@@ -973,10 +985,22 @@ def streamed_e2e(torch, dist, args, wl, job_batches, outputs, flat, my_bytes, al
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    return {"value": wl.total_params / dt / 1e6, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "seconds_per_step": dt, "steps": args.config4_steps, "warmup": 1,
-            "path": "host float16 weights + storage-form Hessians -> per-batch uploads, device decode -> "
-                    "streamed encode -> host bytes"}
+    out = {"value": wl.total_params / dt / 1e6, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h), "seconds_per_step": dt, "steps": args.config4_steps, "warmup": 1,
+           "path": "host float16 weights + storage-form Hessians -> per-batch uploads, device decode -> "
+                   "streamed encode -> host bytes"}
+    if world > 1:
+        out["d2h_path"] = ("each rank's bytes, batch by batch, over its own link into one shared host buffer read "
+                           "by rank 0" if hg is not None else f"NCCL gather to rank 0, then rank 0's copy ({hg_note})")
+    if hg is not None:   # outside the timed region: the host buffer against a device gather
+        bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+        if rank == 0:
+            ref = torch.cat([bb[:bb.numel()].cpu() for bb in bufs])
+            out["host_gather_identical_to_device_gather"] = bool(torch.equal(ref, hg.view[:ref.numel()]))
+            del ref
+        del bufs
+        hg.close()
+    return out
 
 
 def measure_xtx(torch, dist, args, rank, world, local_rank):
@@ -1092,7 +1116,7 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
     in the reference's storage form (float16 / hscale + exact float32 diagonal) copied from
     pinned memory every step, packed bytes copied back to pinned memory."""
     from perm_b200 import _native as nat
-    from perm_b200.shard import gather_to_rank0
+    from perm_b200.shard import HostGather, gather_to_rank0
     # weights: one pinned float16 image of the rank's flat float32 buffer
     host_w = wl.x_flat.to(torch.float16).cpu().pin_memory()
     dev_w16 = torch.empty_like(host_w, device="cuda")
@@ -1120,7 +1144,16 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
     host_d32 = torch.cat(diag_parts).cpu().pin_memory()
     dev_d32 = torch.empty_like(host_d32, device="cuda")
     dev_H = {k: torch.empty_like(wl.hess[k]) for k in keys}
-    host_out = torch.empty(max(1, my_bytes if world == 1 else (sum(all_sizes) if rank == 0 else 0)),
+    # N > 1: every rank copies its packed bytes over its own link into one shared host buffer
+    # (HostGather) that rank 0 reads; without room in /dev/shm, the NCCL gather to rank 0 and
+    # rank 0's copy of all the bytes instead
+    hg, hg_note = None, None
+    if world > 1:
+        try:
+            hg = HostGather(torch, dist, all_sizes, rank, world)
+        except OSError as e:
+            hg_note = str(e)
+    host_out = torch.empty(max(1, my_bytes if world == 1 else (sum(all_sizes) if rank == 0 and hg is None else 0)),
                            dtype=torch.uint8).pin_memory()
     h2d = host_w.numel() * 2 + sum(v.numel() * 2 for v in host_h16.values()) + host_d32.numel() * 4
     d2h = sum(all_sizes) if rank == 0 else 0
@@ -1214,14 +1247,16 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
         weights(chunks[1:])
         hs = {k: dev_H[k] for k in wl.ef_keys}
 
-        def copy_out(ev, _names):   # one GPU: the bytes leave while the statistics run
+        def copy_out(ev, _names):   # the bytes leave while the statistics run
             d2h_stream.wait_event(ev)
             with torch.cuda.stream(d2h_stream):
-                host_out[:my_bytes].copy_(flat[:my_bytes], non_blocking=True)
+                dst = hg.mine if hg is not None else host_out[:my_bytes]
+                dst.copy_(flat[:my_bytes], non_blocking=True)
 
         enc.run(jobs, hs, {k: host_diag[k] for k in wl.ef_keys}, stats=True, outputs=outputs,
-                inputs_event=staged, ready_events=ready, after_pack=copy_out if world == 1 else None)
-        if world > 1:
+                inputs_event=staged, ready_events=ready,
+                after_pack=copy_out if (world == 1 or hg is not None) else None)
+        if world > 1 and hg is None:
             bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
             if rank == 0:
                 off = 0
@@ -1229,6 +1264,8 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
                     host_out[off:off + b.numel()].copy_(b[:b.numel()], non_blocking=True)
                     off += b.numel()
         torch.cuda.synchronize()
+        if hg is not None:
+            hg.barrier()   # every rank's bytes are in rank 0's host buffer
 
     for _ in range(max(1, min(args.warmup, 2))):
         step()
@@ -1242,9 +1279,19 @@ def measure_e2e(torch, dist, args, wl, enc, jobs, outputs, flat, my_bytes, all_s
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    return {"value": wl.total_params / dt / 1e6, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "seconds_per_step": dt,
-            "path": "host float16 weights + stored-form Hessians -> device decode -> encode -> host bytes"}
+    out = {"value": wl.total_params / dt / 1e6, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h), "seconds_per_step": dt,
+           "path": "host float16 weights + stored-form Hessians -> device decode -> encode -> host bytes"}
+    if world > 1:
+        out["d2h_path"] = ("each rank's bytes over its own link into one shared host buffer read by rank 0"
+                           if hg is not None else f"NCCL gather to rank 0, then rank 0's copy ({hg_note})")
+    if hg is not None:   # outside the timed region: the host buffer against a device gather
+        bufs = gather_to_rank0(torch, dist, flat[:my_bytes], all_sizes, rank, world)
+        if rank == 0:
+            ref = torch.cat([b[:b.numel()].cpu() for b in bufs])
+            out["host_gather_identical_to_device_gather"] = bool(torch.equal(ref, hg.view[:ref.numel()]))
+        hg.close()
+    return out
 
 
 def main():

@@ -174,6 +174,87 @@ def gather_stats_to_rank0(dist, stats, rank, world):
     return merge_unit_stats(allst)
 
 
+class HostGather:
+    """One host buffer, in POSIX shared memory, that every rank of a node writes its packed
+    bytes into, each over its own PCIe link.  Rank 0 then holds the whole model's bytes in host
+    memory without a device-side gather and without one link carrying all of them (the
+    alternative to gather_to_rank0 followed by rank 0's device-to-host copy).
+
+    Rank 0 creates the segment (`sizes[r]` bytes per rank, in rank order) and the others attach
+    to it by name.  With `register=True` every rank page-locks the mapping with the CUDA driver
+    (cudaHostRegister), so copies into it can be asynchronous.  Raises OSError when /dev/shm
+    has not the room (the caller then keeps the device gather); every rank makes the same
+    decision, since rank 0 broadcasts it.  After each rank's copies have completed, `barrier()`
+    tells rank 0 that `view` is whole.  `close()` releases the segment on every rank."""
+
+    def __init__(self, torch, dist, sizes, rank, world, register=True):
+        import os
+        from multiprocessing import shared_memory
+        self.torch, self.dist, self.rank, self.world = torch, dist, rank, world
+        self.sizes = [int(v) for v in sizes]
+        self.total = max(1, sum(self.sizes))
+        self.off = sum(self.sizes[:rank])
+        msg = [None]
+        shm = None
+        if rank == 0:
+            try:
+                st = os.statvfs("/dev/shm")
+                if st.f_bavail * st.f_frsize < self.total + (64 << 20):
+                    raise OSError("/dev/shm has not the room for the host gather")
+                shm = shared_memory.SharedMemory(create=True, size=self.total)
+                msg = [shm.name]
+            except OSError as e:
+                msg = ["!" + str(e)]
+        dist.broadcast_object_list(msg, src=0)
+        if msg[0].startswith("!"):
+            raise OSError(msg[0][1:])
+        if rank != 0:
+            shm = shared_memory.SharedMemory(name=msg[0])
+            try:   # the creating rank owns the segment: keep this process's tracker from unlinking it
+                from multiprocessing import resource_tracker
+                resource_tracker.unregister(shm._name, "shared_memory")
+            except Exception:
+                pass
+        self.shm = shm
+        self.view = torch.frombuffer(shm.buf, dtype=torch.uint8)[:self.total]
+        self.mine = self.view[self.off:self.off + self.sizes[rank]]
+        self.registered = False
+        ok = 1
+        if register:
+            rc = int(torch.cuda.cudart().cudaHostRegister(self.view.data_ptr(), self.total, 0))
+            self.registered = rc == 0
+            ok = int(self.registered)
+        # every rank takes the same path: a registration that failed anywhere closes it everywhere
+        flag = torch.tensor([ok], dtype=torch.int32,
+                            device="cuda" if dist.get_backend() == "nccl" else "cpu")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0:
+            self.close()
+            raise OSError("page-locking the host gather buffer failed on a rank")
+
+    def barrier(self):
+        self.dist.barrier()
+
+    def close_local(self):
+        if self.registered:
+            self.torch.cuda.cudart().cudaHostUnregister(self.view.data_ptr())
+            self.registered = False
+        self.view = self.mine = None
+        if self.shm is not None:
+            try:
+                self.shm.close()
+            except BufferError:   # a tensor over the buffer is still alive: unmapped at exit
+                pass
+
+    def close(self):
+        """Every rank unmaps; rank 0 unlinks the segment once the others are done with it."""
+        self.close_local()
+        self.dist.barrier()
+        if self.rank == 0 and self.shm is not None:
+            self.shm.unlink()
+        self.shm = None
+
+
 class RankFailure(RuntimeError):
     """Another rank reported a failure between steps."""
 

@@ -135,6 +135,36 @@ def test_stats_gather_merges_every_rank():
     assert abs(m["output.weight"]["rel_err_vs_stock"] - (6.0 / 6.0 - 1)) < 1e-12
 
 
+def _host_gather_worker(rank, world, port, out):
+    dist = _init(rank, world, port, 60)
+    try:
+        import torch
+        from perm_b200.shard import HostGather
+        sizes = [5, 0, 7]
+        hg = HostGather(torch, dist, sizes, rank, world, register=False)
+        for step in range(2):   # two steps into the same buffer, as in a timed loop
+            hg.mine.copy_(torch.full((sizes[rank],), 10 * step + rank + 1, dtype=torch.uint8))
+            hg.barrier()
+            if rank == 0:
+                out.put(hg.view.tolist())
+            hg.barrier()   # rank 0 has read this step before anyone writes the next
+        hg.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_gather_assembles_every_rank_in_shared_memory():
+    """HostGather: each rank writes its bytes into one shared host buffer (ragged sizes, an
+    empty rank included); after the barrier rank 0 sees them in rank order, step after step."""
+    procs, q = _spawn(_host_gather_worker, 3)
+    got = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for step in range(2):
+        assert got[step] == [10 * step + 1] * 5 + [10 * step + 3] * 7
+
+
 def _failing_worker(rank, world, port, out, fail_rank, fail_step):
     """Steps of one all-reduce each under a RankGuard; `fail_rank` raises between steps."""
     import time
