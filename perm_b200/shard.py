@@ -208,29 +208,34 @@ class HostGather:
         dist.broadcast_object_list(msg, src=0)
         if msg[0].startswith("!"):
             raise OSError(msg[0][1:])
-        if rank != 0:
-            shm = shared_memory.SharedMemory(name=msg[0])
-            try:   # the creating rank owns the segment: keep this process's tracker from unlinking it
-                from multiprocessing import resource_tracker
-                resource_tracker.unregister(shm._name, "shared_memory")
-            except Exception:
-                pass
-        self.shm = shm
-        self.view = torch.frombuffer(shm.buf, dtype=torch.uint8)[:self.total]
-        self.mine = self.view[self.off:self.off + self.sizes[rank]]
-        self.registered = False
         ok = 1
-        if register:
+        if rank != 0:
+            try:
+                shm = shared_memory.SharedMemory(name=msg[0])
+            except OSError:
+                shm, ok = None, 0
+            else:
+                try:   # the creating rank owns the segment: keep this process's tracker from unlinking it
+                    from multiprocessing import resource_tracker
+                    resource_tracker.unregister(shm._name, "shared_memory")
+                except Exception:
+                    pass
+        self.shm = shm
+        self.view = torch.frombuffer(shm.buf, dtype=torch.uint8)[:self.total] if shm is not None else None
+        self.mine = self.view[self.off:self.off + self.sizes[rank]] if shm is not None else None
+        self.registered = False
+        if register and shm is not None:
             rc = int(torch.cuda.cudart().cudaHostRegister(self.view.data_ptr(), self.total, 0))
             self.registered = rc == 0
             ok = int(self.registered)
-        # every rank takes the same path: a registration that failed anywhere closes it everywhere
+        # every rank takes the same path: an attach or a registration that failed anywhere
+        # closes the buffer everywhere
         flag = torch.tensor([ok], dtype=torch.int32,
                             device="cuda" if dist.get_backend() == "nccl" else "cpu")
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if int(flag.item()) == 0:
             self.close()
-            raise OSError("page-locking the host gather buffer failed on a rank")
+            raise OSError("attaching or page-locking the host gather buffer failed on a rank")
 
     def barrier(self):
         self.dist.barrier()
