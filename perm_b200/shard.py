@@ -208,6 +208,9 @@ class HostGather:
         dist.broadcast_object_list(msg, src=0)
         if msg[0].startswith("!"):
             raise OSError(msg[0][1:])
+        if rank == 0:   # a step that raises before close() still leaves no segment behind
+            import atexit
+            atexit.register(HostGather._unlink_quietly, shm.name)
         ok = 1
         if rank != 0:
             try:
@@ -239,6 +242,16 @@ class HostGather:
 
     def barrier(self):
         self.dist.barrier()
+
+    @staticmethod
+    def _unlink_quietly(name):
+        from multiprocessing import shared_memory
+        try:
+            seg = shared_memory.SharedMemory(name=name)
+        except OSError:
+            return   # already unlinked by close()
+        seg.close()
+        seg.unlink()
 
     def close_local(self):
         if self.registered:
